@@ -1,0 +1,154 @@
+// extern "C" boundary of libpolyattn.so: argument validation, kernel choice,
+// thread-local error reporting. Declarations and the reference interfaces
+// each entry point replaces are in include/poly_attention.h.
+#include <cstdlib>
+#include <string>
+
+#include "common.cuh"
+
+namespace poly {
+
+static thread_local std::string g_error;
+
+void set_error(const std::string& msg) { g_error = msg; }
+
+static int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+static bool force_simt() {
+  const char* e = std::getenv("POLY_FORCE_SIMT");
+  return e && e[0] == '1';
+}
+
+static int check_pass(const PolyPassArgs* a) {
+  if (!a) return fail(POLY_EINVAL, "null args");
+  if (a->batch <= 0 || a->heads <= 0 || a->kv_heads <= 0 || a->seq_q < 0 || a->seq_k <= 0 || a->head_dim <= 0)
+    return fail(POLY_EINVAL, "batch, heads, kv_heads, seq_k and head_dim must be positive, seq_q non-negative");
+  if (a->heads % a->kv_heads != 0) return fail(POLY_EINVAL, "heads must be divisible by kv_heads");
+  if (a->dtype != POLY_F32 && a->dtype != POLY_F16 && a->dtype != POLY_BF16) return fail(POLY_EINVAL, "unknown dtype");
+  if (a->head_dim > 128) return fail(POLY_EUNSUPPORTED, "head_dim > 128 is not supported");
+  if (!a->q || !a->k || !a->v || !a->out) return fail(POLY_EINVAL, "q, k, v and out are required");
+  if (a->epi_out && !a->epi_mul) return fail(POLY_EINVAL, "epi_out requires epi_mul");
+  if (!(a->scale == a->scale)) return fail(POLY_EINVAL, "scale is NaN");
+  return POLY_OK;
+}
+
+enum class FwdKind { kSimt, kTc, kDecode };
+
+static FwdKind choose_fwd(const PolyPassArgs& a) {
+  if (force_simt()) return FwdKind::kSimt;
+  if (pass_decode_eligible(a)) return FwdKind::kDecode;
+  if (pass_fwd_tc_eligible(a)) return FwdKind::kTc;
+  return FwdKind::kSimt;
+}
+
+static bool use_bwd_tc(const PolyPassBwdArgs& a) { return !force_simt() && pass_bwd_tc_eligible(a); }
+
+static size_t simt_bwd_workspace(const PolyPassBwdArgs& a) {
+  return (size_t)a.fwd.batch * a.fwd.heads * (size_t)a.fwd.seq_q * sizeof(float);
+}
+
+}  // namespace poly
+
+using namespace poly;
+
+extern "C" {
+
+const char* poly_last_error(void) { return g_error.c_str(); }
+int poly_abi_version(void) { return POLY_ABI_VERSION; }
+size_t poly_sizeof_pass_args(void) { return sizeof(PolyPassArgs); }
+size_t poly_sizeof_pass_bwd_args(void) { return sizeof(PolyPassBwdArgs); }
+size_t poly_sizeof_merge_args(void) { return sizeof(PolyMergeArgs); }
+
+size_t poly_pass_fwd_workspace_size(const PolyPassArgs* a) {
+  if (check_pass(a) != POLY_OK) return 0;
+  switch (choose_fwd(*a)) {
+    case FwdKind::kDecode: return pass_decode_workspace(*a);
+    case FwdKind::kTc: return pass_fwd_tc_workspace(*a);
+    default: return 0;
+  }
+}
+
+const char* poly_pass_fwd_kernel_name(const PolyPassArgs* a) {
+  if (check_pass(a) != POLY_OK) return "invalid";
+  switch (choose_fwd(*a)) {
+    case FwdKind::kDecode: return "decode";
+    case FwdKind::kTc: return "tc100";
+    default: return "simt";
+  }
+}
+
+int poly_pass_fwd(const PolyPassArgs* a, void* stream) {
+  int rc = check_pass(a);
+  if (rc) return rc;
+  if (a->seq_q == 0) return POLY_OK;
+  const FwdKind kind = choose_fwd(*a);
+  size_t need = 0;
+  if (kind == FwdKind::kDecode) need = pass_decode_workspace(*a);
+  if (kind == FwdKind::kTc) need = pass_fwd_tc_workspace(*a);
+  if (need && (!a->workspace || a->workspace_bytes < need))
+    return fail(POLY_EINVAL, "workspace too small: need " + std::to_string(need) + " bytes");
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (kind) {
+    case FwdKind::kDecode: return launch_pass_decode(*a, s);
+    case FwdKind::kTc: return launch_pass_fwd_tc(*a, s);
+    default: return launch_pass_fwd_simt(*a, s);
+  }
+}
+
+size_t poly_pass_bwd_workspace_size(const PolyPassBwdArgs* a) {
+  if (!a || check_pass(&a->fwd) != POLY_OK) return 0;
+  return use_bwd_tc(*a) ? pass_bwd_tc_workspace(*a) : simt_bwd_workspace(*a);
+}
+
+const char* poly_pass_bwd_kernel_name(const PolyPassBwdArgs* a) {
+  if (!a || check_pass(&a->fwd) != POLY_OK) return "invalid";
+  return use_bwd_tc(*a) ? "tc100" : "simt";
+}
+
+int poly_pass_bwd(const PolyPassBwdArgs* a, void* stream) {
+  if (!a) return fail(POLY_EINVAL, "null args");
+  int rc = check_pass(&a->fwd);
+  if (rc) return rc;
+  if (a->fwd.v_mul) return fail(POLY_EUNSUPPORTED, "v_mul is forward-only");
+  if (!a->fwd.lse || !a->dout || !a->dq || !a->dk || !a->dv)
+    return fail(POLY_EINVAL, "backward needs fwd.out, fwd.lse, dout, dq, dk and dv");
+  const bool tc = use_bwd_tc(*a);
+  const size_t need = tc ? pass_bwd_tc_workspace(*a) : simt_bwd_workspace(*a);
+  if (need && (!a->workspace || a->workspace_bytes < need))
+    return fail(POLY_EINVAL, "workspace too small: need " + std::to_string(need) + " bytes");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (a->fwd.seq_q == 0) {
+    // no queries: dk, dv and dbias are zero
+    const size_t es = a->fwd.dtype == POLY_F32 ? 4 : 2;
+    for (int b = 0; b < a->fwd.batch; ++b)
+      for (int h = 0; h < a->fwd.kv_heads; ++h) {
+        char* dk = (char*)a->dk + (b * a->dk_stride[0] + h * a->dk_stride[1]) * es;
+        char* dv = (char*)a->dv + (b * a->dv_stride[0] + h * a->dv_stride[1]) * es;
+        rc = cuda_status(cudaMemset2DAsync(dk, a->dk_stride[2] * es, 0, a->fwd.head_dim * es, a->fwd.seq_k, s), "memset dk");
+        if (rc) return rc;
+        rc = cuda_status(cudaMemset2DAsync(dv, a->dv_stride[2] * es, 0, a->fwd.head_dim * es, a->fwd.seq_k, s), "memset dv");
+        if (rc) return rc;
+        if (a->dbias) {
+          rc = cuda_status(cudaMemsetAsync(a->dbias + b * a->dbias_stride[0] + h * a->dbias_stride[1], 0,
+                                           a->fwd.seq_k * sizeof(float), s), "memset dbias");
+          if (rc) return rc;
+        }
+      }
+    return POLY_OK;
+  }
+  return tc ? launch_pass_bwd_tc(*a, s) : launch_pass_bwd_simt(*a, s);
+}
+
+int poly_lse_merge(const PolyMergeArgs* a, void* stream) {
+  if (!a) return fail(POLY_EINVAL, "null args");
+  if (a->parts <= 0 || a->head_dim <= 0 || a->rows < 0) return fail(POLY_EINVAL, "bad merge sizes");
+  if (!a->part_out || !a->part_lse || !a->out) return fail(POLY_EINVAL, "merge needs part_out, part_lse and out");
+  if (a->dtype != POLY_F32 && a->dtype != POLY_F16 && a->dtype != POLY_BF16) return fail(POLY_EINVAL, "unknown dtype");
+  if (a->rows == 0) return POLY_OK;
+  return launch_lse_merge(*a, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,212 @@
+"""Poly-attention cores built from the single-pass kernel.
+
+* ``poly_attention_order2`` -- both passes of order-2 poly attention with
+  autograd (the work of PolyFlashAttention,
+  poly_attention/flash_poly_attention.py:319-446, and of
+  reference_poly_attention, poly_attention/poly_attention.py:48-116).
+* ``poly_attention_chain`` -- the order-n right-to-left chain
+  (n_poly_attention.py:263-313) with autograd.
+* ``flash_poly_attention`` -- the reference's function-level entry point
+  (poly_attention/flash_poly_attention.py:448-456), same signature.
+
+Key/value-side tensors (q2, q3, v3, ...) may carry fewer heads than q1
+(grouped-query attention): every pass whose queries and keys are both
+key/value tensors runs once per key/value head, and only the last pass reads
+q1 at full head count. The reference repeats those tensors r times instead
+(poly_attention/poly_attention.py:289-293); the results are identical.
+"""
+from __future__ import annotations
+
+import torch
+
+from .ops import pass_bwd, pass_fwd
+
+
+def _exists(v):
+    return v is not None
+
+
+class _Order2(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, softclamp, causal):
+        shared = q2_pass1 is None
+        qp1 = q2 if shared else q2_pass1
+        # pass 1: q2 attends q3 (poly_attention/poly_attention.py:63-82)
+        msg, lse23 = pass_fwd(qp1, q3, v3, causal=causal, softclamp=softclamp, key_mask=cm2)
+        # pass 2: q1 attends q2 with lse23 as key bias (:91-114)
+        out, lse12 = pass_fwd(q1, q2, msg, causal=causal, softclamp=softclamp, bias=lse23, key_mask=cm1,
+                              query_mask=mask)
+        ctx.save_for_backward(q1, q2, q3, v3, qp1, msg, lse23, out, lse12, mask, cm1, cm2)
+        ctx.shared, ctx.softclamp, ctx.causal = shared, softclamp, causal
+        ctx.mark_non_differentiable(lse23, msg)
+        return out, lse23, msg
+
+    @staticmethod
+    def backward(ctx, dout, _dlse, _dmsg):
+        q1, q2, q3, v3, qp1, msg, lse23, out, lse12, mask, cm1, cm2 = ctx.saved_tensors
+        sc, causal = ctx.softclamp, ctx.causal
+        # pass-2 backward: dq1, dq2 (as keys), dmsg (as values), dlse23 (key-bias grad)
+        dq1, dq2_keys, dmsg, dlse23 = pass_bwd(q1, q2, msg, out, lse12, dout, causal=causal, softclamp=sc,
+                                               bias=lse23, key_mask=cm1, query_mask=mask, want_dbias=True)
+        # pass-1 backward with the log-sum-exp gradient folded in; dq2 parts summed in-kernel
+        if ctx.shared:
+            dq2, dq3, dv3, _ = pass_bwd(qp1, q3, v3, msg, lse23, dmsg, causal=causal, softclamp=sc, key_mask=cm2,
+                                        dlse=dlse23, dq=dq2_keys, dq_accumulate=True)
+            return dq1, dq2, dq3, dv3, None, None, None, None, None, None
+        dqp1, dq3, dv3, _ = pass_bwd(qp1, q3, v3, msg, lse23, dmsg, causal=causal, softclamp=sc, key_mask=cm2,
+                                     dlse=dlse23)
+        return dq1, dq2_keys, dq3, dv3, dqp1, None, None, None, None, None
+
+
+def poly_attention_order2(q1, q2, q3, v3, *, q2_pass1=None, mask=None, context_mask=None, softclamp_value=None,
+                          causal=False):
+    """Order-2 poly attention without cache. Returns (out, lse23, msg).
+
+    q1 [b, h, n, d]; q2, q3, v3 [b, g, nk, d] (g divides h). ``q2_pass1``
+    (default q2) is pass 1's query; ``mask`` masks queries of pass 2 and
+    ``context_mask = (cm1, cm2)`` masks keys of pass 2 / pass 1, exactly as in
+    reference_poly_attention. lse23 / msg are at g heads.
+    """
+    cm1, cm2 = context_mask if _exists(context_mask) else (None, None)
+    return _Order2.apply(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, softclamp_value, bool(causal))
+
+
+def poly_attention_order2_cached(q1, q2_new, q2_full, q3_full, v3_full, lse_cache, msg_cache, *,
+                                 softclamp_value=None, context_mask=None, mask=None):
+    """One KV-cache step of order 2 (poly_attention/poly_attention.py:84-87,
+    283-287): pass 1 for the new rows against the full cache, then pass 2 of
+    q1 against q2_full with the concatenated (lse23, msg). No causal mask, as
+    in the reference when a cache is given. Returns (out, lse23_step, msg_step).
+    """
+    cm1, cm2 = context_mask if _exists(context_mask) else (None, None)
+    msg_step, lse_step = pass_fwd(q2_new, q3_full, v3_full, softclamp=softclamp_value, key_mask=cm2)
+    lse = lse_step if lse_cache is None else torch.cat((lse_cache.float(), lse_step), -1)
+    msg = msg_step if msg_cache is None else torch.cat((msg_cache, msg_step), -2)
+    out, _ = pass_fwd(q1, q2_full, msg, softclamp=softclamp_value, bias=lse, key_mask=cm1, query_mask=mask)
+    return out, lse_step, msg_step
+
+
+class _Chain(torch.autograd.Function):
+    """Order-n chain. Inputs: order query tensors ``ql`` (queries of each
+    score), order key tensors ``qr`` and order-1 value tensors ``vs``."""
+
+    @staticmethod
+    def forward(ctx, order, softclamp, causal, mask, cms, *tensors):
+        ql = list(tensors[:order])
+        qr = list(tensors[order:2 * order])
+        vs = list(tensors[2 * order:])
+        vals, biases, msgs, lses, outs = [None] * order, [None] * order, [None] * order, [None] * order, [None] * order
+        val, bias = vs[-1], None
+        for t in range(order - 1, 0, -1):
+            vals[t], biases[t] = val, bias
+            if t >= 2:
+                # V' = v * msg fused into the epilogue (n_poly_attention.py:287)
+                msg, lse, nxt = pass_fwd(ql[t], qr[t], val, causal=causal, softclamp=softclamp, bias=bias,
+                                         key_mask=cms[t], epi_mul=vs[t - 2])
+            else:
+                msg, lse = pass_fwd(ql[t], qr[t], val, causal=causal, softclamp=softclamp, bias=bias,
+                                    key_mask=cms[t])
+                nxt = msg
+            msgs[t], lses[t] = msg, lse
+            val, bias = nxt, lse
+        vals[0], biases[0] = val, bias
+        out, lse0 = pass_fwd(ql[0], qr[0], val, causal=causal, softclamp=softclamp, bias=bias, key_mask=cms[0],
+                             query_mask=mask)
+        outs[0], lses[0] = out, lse0
+        ctx.order, ctx.softclamp, ctx.causal = order, softclamp, causal
+        ctx.cms, ctx.mask = cms, mask
+        ctx.save_for_backward(*ql, *qr, *vs, *[v for v in vals], *[b if b is not None else torch.empty(0) for b in biases],
+                              *[m if m is not None else torch.empty(0) for m in msgs], *lses, out)
+        # caches in the reference's order (level order-1 first, level 1 last)
+        new_lses = tuple(lses[t] for t in range(order - 1, 0, -1))
+        new_msgs = tuple(msgs[t] for t in range(order - 1, 0, -1))
+        ctx.mark_non_differentiable(*new_lses, *new_msgs)
+        return (out, *new_lses, *new_msgs)
+
+    @staticmethod
+    def backward(ctx, dout, *_unused):
+        n = ctx.order
+        st = ctx.saved_tensors
+        ql, qr, vs = list(st[:n]), list(st[n:2 * n]), list(st[2 * n:3 * n - 1])
+        o = 3 * n - 1
+        vals = list(st[o:o + n]); o += n
+        biases = [b if b.numel() else None for b in st[o:o + n]]; o += n
+        msgs = [m if m.numel() else None for m in st[o:o + n]]; o += n
+        lses = list(st[o:o + n]); o += n
+        outs = [st[o]] + [msgs[t] for t in range(1, n)]
+        dql, dqr, dvs = [None] * n, [None] * n, [None] * (n - 1)
+        g_out, g_lse = dout, None
+        for t in range(n):
+            dq, dk, dv, db = pass_bwd(ql[t], qr[t], vals[t], outs[t], lses[t], g_out, causal=ctx.causal,
+                                      softclamp=ctx.softclamp, bias=biases[t], key_mask=ctx.cms[t],
+                                      query_mask=ctx.mask if t == 0 else None, dlse=g_lse,
+                                      want_dbias=t < n - 1)
+            dql[t], dqr[t] = dq, dk
+            if t == n - 1:
+                dvs[-1] = dv
+                break
+            if t == 0:
+                g_out = dv
+            else:
+                dvs[t - 1] = dv * msgs[t + 1]
+                g_out = dv * vs[t - 1]
+            g_lse = db
+        return (None, None, None, None, None, *dql, *dqr, *dvs)
+
+
+def poly_attention_chain(q_left, q_right, vs, *, softclamp_value=None, causal=False, mask=None, context_masks=None):
+    """Order-n chain without cache (n = len(q_left)).
+
+    q_left[0] = q1 [b, h, n, d]; q_left[t >= 1], q_right[t], vs[t] are
+    key/value-side tensors [b, g, n, d]. Returns (out, lses, msgs) with lses /
+    msgs in the reference's cache order.
+    """
+    order = len(q_left)
+    cms = tuple(context_masks) if context_masks is not None else (None,) * order
+    res = _Chain.apply(order, softclamp_value, bool(causal), mask, cms, *q_left, *q_right, *vs)
+    return res[0], res[1:order], res[order:]
+
+
+def poly_attention_chain_cached(q_left, q_right_full, vs_full, cache_lses, cache_msgs, *, softclamp_value=None,
+                                mask=None, context_masks=None):
+    """One KV-cache step of the order-n chain (n_poly_attention.py:265-313).
+
+    The values of level t >= 1 are vs_full[t-1] * msg_full of level t+1; the
+    product is taken inside the kernel from the two cached tensors (v_mul), so
+    no full-length V' is materialised. Returns (out, new_lse_steps,
+    new_msg_steps) in the reference's cache order.
+    """
+    order = len(q_left)
+    cms = tuple(context_masks) if context_masks is not None else (None,) * order
+    val, vmul, bias = vs_full[-1], None, None
+    step_lses, step_msgs = [], []
+    for t in range(order - 1, 0, -1):
+        idx = (order - 1) - t
+        msg_step, lse_step = pass_fwd(q_left[t], q_right_full[t], val, softclamp=softclamp_value, bias=bias,
+                                      key_mask=cms[t], v_mul=vmul)
+        step_lses.append(lse_step)
+        step_msgs.append(msg_step)
+        lse_full = lse_step if cache_lses is None else torch.cat((cache_lses[idx].float(), lse_step), -1)
+        msg_full = msg_step if cache_msgs is None else torch.cat((cache_msgs[idx], msg_step), -2)
+        bias = lse_full
+        if t >= 2:
+            val, vmul = vs_full[t - 2], msg_full
+        else:
+            val, vmul = msg_full, None
+    out, _ = pass_fwd(q_left[0], q_right_full[0], val, softclamp=softclamp_value, bias=bias, key_mask=cms[0],
+                      query_mask=mask, v_mul=vmul)
+    return out, step_lses, step_msgs
+
+
+def flash_poly_attention(q1, q2, q3, v3, mask=None, context_mask=None, softclamp_value=None, is_causal=True):
+    """Drop-in for poly_attention/flash_poly_attention.py:448-456.
+
+    Same arguments and error behaviour: ``context_mask`` is rejected with the
+    reference's AssertionError; ``mask`` [b, n] masks keys in both passes.
+    q2 / q3 / v3 may have fewer heads than q1 (grouped-query attention).
+    """
+    assert not _exists(context_mask), 'context_mask is not supported in flash_poly_attention'
+    cm = (mask, mask) if _exists(mask) else None
+    out, _, _ = poly_attention_order2(q1, q2, q3, v3, context_mask=cm, softclamp_value=softclamp_value,
+                                      causal=is_causal)
+    return out

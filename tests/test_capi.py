@@ -1,0 +1,95 @@
+"""CPU checks of the C-ABI library: it loads, exports every symbol that
+include/poly_attention.h declares, agrees on struct layouts, and the product
+path refuses CPU tensors (there is no CPU implementation)."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "poly_attention.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    return re.findall(r"POLY_API\s+[\w\s\*]+?\b(poly_\w+)\s*\(", src)
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert {"poly_pass_fwd", "poly_pass_bwd", "poly_lse_merge", "poly_last_error"} <= set(names)
+
+
+def test_library_exports_every_declared_symbol():
+    from poly_attention_b200 import _lib
+    for name in declared():
+        assert hasattr(_lib.lib, name), name
+        assert name in _lib.EXPORTS, f"{name} is not bound in _lib.EXPORTS"
+
+
+def test_struct_layout_matches():
+    from poly_attention_b200 import _lib
+    assert _lib.lib.poly_sizeof_pass_args() == ctypes.sizeof(_lib.PolyPassArgs)
+    assert _lib.lib.poly_sizeof_pass_bwd_args() == ctypes.sizeof(_lib.PolyPassBwdArgs)
+    assert _lib.lib.poly_sizeof_merge_args() == ctypes.sizeof(_lib.PolyMergeArgs)
+    assert _lib.lib.poly_abi_version() == _lib.ABI_VERSION
+
+
+def test_invalid_args_report_errors_without_gpu():
+    from poly_attention_b200 import _lib
+    a = _lib.PolyPassArgs()
+    rc = _lib.lib.poly_pass_fwd(ctypes.byref(a), None)
+    assert rc == _lib.POLY_EINVAL
+    assert "positive" in _lib.lib.poly_last_error().decode()
+    a.batch = a.heads = a.kv_heads = a.seq_q = a.seq_k = 1
+    a.head_dim, a.heads, a.kv_heads = 64, 3, 2
+    assert _lib.lib.poly_pass_fwd(ctypes.byref(a), None) == _lib.POLY_EINVAL
+    assert "divisible" in _lib.lib.poly_last_error().decode()
+    a.heads, a.head_dim = 2, 512
+    assert _lib.lib.poly_pass_fwd(ctypes.byref(a), None) == _lib.POLY_EUNSUPPORTED
+
+
+def test_product_path_refuses_cpu_tensors():
+    import poly_attention_b200 as P
+    q = torch.randn(1, 2, 8, 32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        P.flash_poly_attention(q, q, q, q)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        P.PolyAttention(dim=64, heads=2, dim_head=32)(torch.randn(1, 8, 64))
+
+
+def test_flash_rejects_context_mask_like_reference():
+    # poly_attention/flash_poly_attention.py:455 ; tests/test_poly_attention.py:541-552
+    import poly_attention_b200 as P
+    q = torch.randn(2, 4, 16, 32)
+    cm = (torch.ones(2, 16, dtype=torch.bool), torch.ones(2, 16, dtype=torch.bool))
+    with pytest.raises(AssertionError, match="context_mask is not supported"):
+        P.flash_poly_attention(q, q, q, q, context_mask=cm)
+
+
+def test_module_error_contracts():
+    # tests/test_poly_attention.py:578-586 and the constructor asserts
+    import poly_attention_b200 as P
+    attn = P.PolyAttention(dim=64, heads=4, multiply_root_value=True)
+    x = torch.randn(2, 16, 64)
+    with pytest.raises(AssertionError, match="first context sequence length"):
+        attn(x, context=(torch.randn(2, 20, 64), torch.randn(2, 24, 64)))
+    with pytest.raises(AssertionError, match="divisible"):
+        P.PolyAttention(dim=64, heads=4, kv_heads=3)
+    with pytest.raises(AssertionError, match="root value"):
+        P.NPolyAttention(dim=64, heads=4, kv_heads=2, use_root_value_as_attn_gate=True)
+
+
+def test_state_dict_names_match_reference(golden):
+    import poly_attention_b200 as P
+    g = golden("mod2_causal_gqa")
+    ref_keys = {k[2:] for k in g if k.startswith("p:")}
+    m = P.PolyAttention(dim=64, heads=4, kv_heads=2, dim_head=16, causal=True, softclamp_value=20.0)
+    assert set(m.state_dict()) == ref_keys
+    g = golden("modn_o3_g2")
+    ref_keys = {k[2:] for k in g if k.startswith("p:")}
+    m = P.NPolyAttention(dim=64, order=3, heads=4, kv_heads=2, dim_head=16, causal=True)
+    assert set(m.state_dict()) == ref_keys
