@@ -64,7 +64,9 @@ extern "C" {
  *   out_i = softmax_j(s_ij) v_j ,  lse_i = logsumexp_j s_ij
  *
  * A row whose every entry is excluded gets the reference's value for it: the
- * uniform average of v over all seq_k keys, lse = -FLT_MAX.
+ * uniform average of v over its keys (all keys except those both masked and
+ * "dead", i.e. with bias <= -FLT_MAX/2, where the reference overflows to
+ * -inf), lse = -FLT_MAX.
  *
  * Optional value multiplier (forward only): if v_mul != NULL the pass uses
  * v_j * v_mul_j as its values, so a decode step reads the order-n chain's

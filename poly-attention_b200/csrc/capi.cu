@@ -47,7 +47,7 @@ static FwdKind choose_fwd(const PolyPassArgs& a) {
 static bool use_bwd_tc(const PolyPassBwdArgs& a) { return !force_simt() && pass_bwd_tc_eligible(a); }
 
 static size_t simt_bwd_workspace(const PolyPassBwdArgs& a) {
-  return (size_t)a.fwd.batch * a.fwd.heads * (size_t)a.fwd.seq_q * sizeof(float);
+  return (size_t)a.fwd.batch * a.fwd.heads * (size_t)a.fwd.seq_q * (sizeof(float) + sizeof(int));
 }
 
 }  // namespace poly

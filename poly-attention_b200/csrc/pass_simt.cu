@@ -40,6 +40,15 @@ __device__ __forceinline__ void load_tile(float (*dst)[DMAX + 1], const T* base,
   }
 }
 
+// In a fully excluded row, does key j take part in the reference's uniform
+// average? Yes unless it is masked (causal / key / query) and dead at once.
+__device__ __forceinline__ bool fallback_key(const PolyPassArgs& a, int i, int j, bool q_masked,
+                                             const uint8_t* km, const float* bias, int seq_k) {
+  const bool masked = q_masked || (a.causal && j > i) || (km && km[j] == 0);
+  const bool dead = bias && bias[j] <= kDeadBias;
+  return !(masked && dead);
+}
+
 template <typename T, int DMAX>
 __global__ void __launch_bounds__(kWarps * 32) pass_fwd_simt_kernel(const PolyPassArgs a) {
   constexpr int NT = DMAX / 32;
@@ -115,10 +124,15 @@ __global__ void __launch_bounds__(kWarps * 32) pass_fwd_simt_kernel(const PolyPa
 
   float lse;
   if (m == -INFINITY) {
-    // every entry excluded: uniform average over all keys (reference semantics)
+    // Every entry excluded: the reference's -finfo.max fill makes the row a
+    // uniform average over its keys, except keys that are both masked and
+    // dead (-max + -max overflows to -inf there).
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    int count = 0;
     for (int j = 0; j < a.seq_k; ++j) {
+      if (!fallback_key(a, i, j, q_masked, km, bias, a.seq_k)) continue;
+      ++count;
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const int col = lane + 32 * t;
@@ -129,7 +143,7 @@ __global__ void __launch_bounds__(kWarps * 32) pass_fwd_simt_kernel(const PolyPa
         }
       }
     }
-    const float inv = 1.f / (float)a.seq_k;
+    const float inv = count ? 1.f / (float)count : 0.f;
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t] *= inv;
     lse = -FLT_MAX;
@@ -158,7 +172,7 @@ __global__ void __launch_bounds__(kWarps * 32) pass_fwd_simt_kernel(const PolyPa
 // delta_i = dout_i . out_i - dlse_i  (the row term of ds; dlse folds in the
 // log-sum-exp gradient, poly_attention/flash_poly_attention.py:280-284)
 template <typename T>
-__global__ void bwd_delta_kernel(const PolyPassBwdArgs a, float* delta) {
+__global__ void bwd_delta_kernel(const PolyPassBwdArgs a, float* delta, int* fb_count) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int rows = a.fwd.batch * a.fwd.heads * a.fwd.seq_q;
   if (warp >= rows) return;
@@ -169,9 +183,20 @@ __global__ void bwd_delta_kernel(const PolyPassBwdArgs a, float* delta) {
   float s = 0.f;
   for (int t = lane; t < a.fwd.head_dim; t += 32) s += to_f32(o[t]) * to_f32(g[t]);
   s = warp_sum(s);
+  const float lse_i = a.fwd.lse[b * a.fwd.lse_stride[0] + h * a.fwd.lse_stride[1] + i];
+  int count = 0;
+  if (lse_i <= kDeadBias) {
+    const int kvh = h / (a.fwd.heads / a.fwd.kv_heads);
+    const float* bias = a.fwd.bias ? a.fwd.bias + b * a.fwd.bias_stride[0] + kvh * a.fwd.bias_stride[1] : nullptr;
+    const uint8_t* km = a.fwd.key_mask ? a.fwd.key_mask + b * a.fwd.key_mask_stride : nullptr;
+    const bool qm = a.fwd.query_mask && a.fwd.query_mask[b * a.fwd.query_mask_stride + i] == 0;
+    for (int j = lane; j < a.fwd.seq_k; j += 32) count += fallback_key(a.fwd, i, j, qm, km, bias, a.fwd.seq_k);
+    for (int o = 16; o > 0; o >>= 1) count += __shfl_xor_sync(0xffffffffu, count, o);
+  }
   if (lane == 0) {
     if (a.dlse) s -= a.dlse[b * a.dlse_stride[0] + h * a.dlse_stride[1] + i];
     delta[warp] = s;
+    fb_count[warp] = count;
   }
 }
 
@@ -183,7 +208,7 @@ struct Entry {
 };
 
 __device__ __forceinline__ Entry bwd_entry(const PolyPassArgs& a, float dot, int i, int j, bool q_masked,
-                                           bool k_masked, const float* bias, float lse_i) {
+                                           bool k_masked, const float* bias, float lse_i, int fb_count) {
   Entry e;
   float s = dot * a.scale;
   e.dfac = 1.f;
@@ -201,8 +226,13 @@ __device__ __forceinline__ Entry bwd_entry(const PolyPassArgs& a, float dot, int
   if (i >= a.seq_q || j >= a.seq_k) {
     e.p = 0.f;
   } else if (lse_i <= kDeadBias) {
-    e.p = 1.f / (float)a.seq_k;   // fully excluded row: uniform over all keys
-    e.keep = false;
+    // fully excluded row: the reference's uniform average (see fallback_key)
+    const bool masked = q_masked || k_masked || (a.causal && j > i);
+    const bool dead = bias && bias[j] <= kDeadBias;
+    e.p = (!(masked && dead) && fb_count > 0) ? 1.f / (float)fb_count : 0.f;
+    // unmasked entries (dead only) still pass gradient to their score, as
+    // autograd through the reference's masked_fill + add does
+    e.keep = !masked;
   } else {
     e.p = e.keep ? exp2f((s + bj - lse_i) * kLog2e) : 0.f;
   }
@@ -210,7 +240,7 @@ __device__ __forceinline__ Entry bwd_entry(const PolyPassArgs& a, float dot, int
 }
 
 template <typename T, int DMAX>
-__global__ void __launch_bounds__(kWarps * 32) pass_bwd_dq_simt_kernel(const PolyPassBwdArgs ab, const float* delta) {
+__global__ void __launch_bounds__(kWarps * 32) pass_bwd_dq_simt_kernel(const PolyPassBwdArgs ab, const float* delta, const int* fb_count) {
   constexpr int NT = DMAX / 32;
   const PolyPassArgs& a = ab.fwd;
   __shared__ float Ks[kTile][DMAX + 1];
@@ -234,6 +264,7 @@ __global__ void __launch_bounds__(kWarps * 32) pass_bwd_dq_simt_kernel(const Pol
   }
   const float lse_i = row_ok ? a.lse[c.b * a.lse_stride[0] + c.h * a.lse_stride[1] + i] : 0.f;
   const float del = row_ok ? delta[((int64_t)blockIdx.y * a.seq_q) + i] : 0.f;
+  const int fbc = row_ok ? fb_count[((int64_t)blockIdx.y * a.seq_q) + i] : 0;
   float acc[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t] = 0.f;
@@ -252,7 +283,7 @@ __global__ void __launch_bounds__(kWarps * 32) pass_bwd_dq_simt_kernel(const Pol
       dp = fmaf(Gs[warp][t], Vs[lane][t], dp);
     }
     const bool k_masked = km && j < a.seq_k && km[j] == 0;
-    const Entry e = bwd_entry(a, dot, i, j, q_masked, k_masked, bias, lse_i);
+    const Entry e = bwd_entry(a, dot, i, j, q_masked, k_masked, bias, lse_i, fbc);
     const float dz = e.keep ? e.p * (dp - del) * e.dfac : 0.f;
 #pragma unroll 4
     for (int jj = 0; jj < kTile; ++jj) {
@@ -275,7 +306,7 @@ __global__ void __launch_bounds__(kWarps * 32) pass_bwd_dq_simt_kernel(const Pol
 }
 
 template <typename T, int DMAX>
-__global__ void __launch_bounds__(kWarps * 32) pass_bwd_dkv_simt_kernel(const PolyPassBwdArgs ab, const float* delta) {
+__global__ void __launch_bounds__(kWarps * 32) pass_bwd_dkv_simt_kernel(const PolyPassBwdArgs ab, const float* delta, const int* fb_count) {
   constexpr int NT = DMAX / 32;
   const PolyPassArgs& a = ab.fwd;
   __shared__ float Qt[kTile][DMAX + 1];
@@ -284,6 +315,7 @@ __global__ void __launch_bounds__(kWarps * 32) pass_bwd_dkv_simt_kernel(const Po
   __shared__ float Vr[kWarps][DMAX];
   __shared__ float lse_t[kTile], del_t[kTile];
   __shared__ uint8_t qm_t[kTile];
+  __shared__ int fb_t[kTile];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.y / a.kv_heads, kvh = blockIdx.y - b * a.kv_heads;
   const int rep = a.heads / a.kv_heads;
@@ -315,6 +347,7 @@ __global__ void __launch_bounds__(kWarps * 32) pass_bwd_dkv_simt_kernel(const Po
         const bool ok = ii < a.seq_q;
         lse_t[threadIdx.x] = ok ? a.lse[b * a.lse_stride[0] + h * a.lse_stride[1] + ii] : 0.f;
         del_t[threadIdx.x] = ok ? delta[((int64_t)(b * a.heads + h) * a.seq_q) + ii] : 0.f;
+        fb_t[threadIdx.x] = ok ? fb_count[((int64_t)(b * a.heads + h) * a.seq_q) + ii] : 0;
         qm_t[threadIdx.x] = (ok && a.query_mask) ? (a.query_mask[b * a.query_mask_stride + ii] == 0) : 0;
       }
       __syncthreads();
@@ -326,7 +359,7 @@ __global__ void __launch_bounds__(kWarps * 32) pass_bwd_dkv_simt_kernel(const Po
         dot = fmaf(Qt[lane][t], Kr[warp][t], dot);
         dp = fmaf(Gt[lane][t], Vr[warp][t], dp);
       }
-      const Entry e = bwd_entry(a, dot, i, j, qm_t[lane] != 0, k_masked, bias, lse_t[lane]);
+      const Entry e = bwd_entry(a, dot, i, j, qm_t[lane] != 0, k_masked, bias, lse_t[lane], fb_t[lane]);
       const float ds = e.p * (dp - del_t[lane]);
       db += (i < a.seq_q) ? ds : 0.f;
       const float dz = e.keep ? ds * e.dfac : 0.f;
@@ -366,13 +399,14 @@ int launch_fwd_t(const PolyPassArgs& a, cudaStream_t s) {
 
 template <typename T, int DMAX>
 int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
-  float* delta = (float*)a.workspace;
   const int rows = a.fwd.batch * a.fwd.heads * a.fwd.seq_q;
-  bwd_delta_kernel<T><<<(rows + 7) / 8, 256, 0, s>>>(a, delta);
+  float* delta = (float*)a.workspace;
+  int* fb_count = (int*)(delta + rows);
+  bwd_delta_kernel<T><<<(rows + 7) / 8, 256, 0, s>>>(a, delta, fb_count);
   dim3 gq((a.fwd.seq_q + kWarps - 1) / kWarps, a.fwd.batch * a.fwd.heads);
-  pass_bwd_dq_simt_kernel<T, DMAX><<<gq, kWarps * 32, 0, s>>>(a, delta);
+  pass_bwd_dq_simt_kernel<T, DMAX><<<gq, kWarps * 32, 0, s>>>(a, delta, fb_count);
   dim3 gk((a.fwd.seq_k + kWarps - 1) / kWarps, a.fwd.batch * a.fwd.kv_heads);
-  pass_bwd_dkv_simt_kernel<T, DMAX><<<gk, kWarps * 32, 0, s>>>(a, delta);
+  pass_bwd_dkv_simt_kernel<T, DMAX><<<gk, kWarps * 32, 0, s>>>(a, delta, fb_count);
   return cuda_status(cudaGetLastError(), "pass_bwd_simt launch");
 }
 

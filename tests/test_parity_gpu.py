@@ -268,3 +268,22 @@ def test_lse_merge_equals_full_pass():
     out, lse = P.lse_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]))
     assert_close(out, host(full), torch.float32)
     assert_close(lse, host(lse_full), torch.float32)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("n", [300, 1024])
+def test_tc_forward_selected_and_matches(d, causal, n):
+    """bf16 / fp16 with d in {64, 128} must run the tcgen05 kernel."""
+    import poly_attention_b200 as P
+    for dtype in (torch.bfloat16, torch.float16):
+        b, h, g = 1, 4, 2
+        q = quant(rnd((b, h, n, d), 1), dtype)
+        k, v = (quant(rnd((b, g, n, d), s), dtype) for s in (2, 3))
+        bias = rnd((b, g, n), 4)
+        qt, kt, vt = dev(q, dtype), dev(k, dtype), dev(v, dtype)
+        assert P.kernel_names(qt, kt, vt, causal=causal)[0] == "tc100"
+        out, lse = P.pass_fwd(qt, kt, vt, causal=causal, bias=dev(bias))
+        eo, el = O.pass_fwd(q, np.repeat(k, 2, 1), np.repeat(v, 2, 1), causal=causal, bias=np.repeat(bias, 2, 1))
+        assert_close(out, eo, dtype, f"out {dtype}")
+        assert_close(lse, el, dtype, f"lse {dtype}")
