@@ -1,0 +1,304 @@
+"""Benchmark of the poly-attention hot path on B200.
+
+Workload (the headline metric's configuration): order-2 causal poly
+attention forward + backward, bf16, batch 8 x 16 heads x seq 4096 x
+dim_head 64 (the attention core of PolyAttention(dim=1024, heads=16,
+dim_head=64, causal=True)). One step = pass 1 + pass 2 forward, then pass 2 +
+pass 1 backward, over synthetic N(0, 1) inputs resident in HBM (4 inputs + dO,
+67 MB each, together larger than the 126 MB L2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs the full per-GPU
+workload on its own batch (batch x head sharding, no collective), so total
+work grows with N ("weak"); time is the max over ranks.
+
+The reference arm (--impl reference) times the CPU restatement of the
+reference algorithm (oracle/poly_oracle.py, numpy, all host threads) on a
+bounded sample: one (batch, head) unit of the same workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "poly-attention_b200"))
+
+METRIC = "order-2 poly-attn fwd+bwd tokens/s/GPU @4K ctx (% bf16 peak); decode tok/s"
+B, H, N, D = 8, 16, 4096, 64
+
+
+def pass_fwd_flop(b):
+    """Algorithmic FLOPs of one causal pass forward: 2 GEMMs of 2*n*n*d/2 per (b, h)."""
+    return 2 * 2 * (N * N / 2) * D * b * H
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            pk = json.load(f)
+        return pk["bf16_tflops_sustained"], pk["bf16_tflops"], pk["hbm_gbs"], "measured"
+    return 1400.0, 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(device, seed, b):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    return [torch.randn(b, H, N, D, device=device, dtype=torch.bfloat16, generator=g) for _ in range(5)]
+
+
+def step_device(P, q1, q2, q3, v3, do, ev=None):
+    """One forward + backward of both passes through the library's pass API."""
+    if ev is not None:
+        ev[0].record()
+    msg, lse23 = P.pass_fwd(q2, q3, v3, causal=True)
+    if ev is not None:
+        ev[1].record()
+    out, lse12 = P.pass_fwd(q1, q2, msg, causal=True, bias=lse23)
+    if ev is not None:
+        ev[2].record()
+    _, dq2, dmsg, dlse23 = P.pass_bwd(q1, q2, msg, out, lse12, do, causal=True, bias=lse23, want_dbias=True)
+    if ev is not None:
+        ev[3].record()
+    P.pass_bwd(q2, q3, v3, msg, lse23, dmsg, causal=True, dlse=dlse23, dq=dq2, dq_accumulate=True)
+    if ev is not None:
+        ev[4].record()
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import poly_attention_b200 as P
+    from poly_attention_b200 import _lib
+
+    b = args.batch
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    q1, q2, q3, v3, do = make_inputs(dev, 1234 + rank, b)
+    for _ in range(args.warmup):
+        step_device(P, q1, q2, q3, v3, do)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # device-resident timed region: K steps between two events
+    n0 = _lib.launch_count()
+    per = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            step_device(P, q1, q2, q3, v3, do, per[i])
+        end.record()
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    phases = [statistics.median(e[k].elapsed_time(e[k + 1]) for e in per) for k in range(4)]
+    t = torch.tensor([start.elapsed_time(end)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # end to end through the public API: host (pinned) inputs in, gradients out
+    e2e = None
+    if not args.no_e2e:
+        hosts = [x.cpu().pin_memory() for x in (q1, q2, q3, v3, do)]
+        grads_h = [torch.empty_like(hosts[0]).pin_memory() for _ in range(4)]
+
+        def e2e_step():
+            d_in = [h.to(dev, non_blocking=True) for h in hosts]
+            ts = [x.requires_grad_(True) for x in d_in[:4]]
+            out = P.flash_poly_attention(*ts, is_causal=True)
+            out.backward(d_in[4])
+            for gh, tt in zip(grads_h, ts):
+                gh.copy_(tt.grad, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        k2 = max(1, min(args.steps, 5))
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(k2):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([s2.elapsed_time(e2) / k2], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": b * N * world / (float(te.item()) * 1e-3), "unit": "tokens/s",
+               "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h in hosts),
+               "d2h_bytes_per_step": sum(g.numel() * g.element_size() for g in grads_h)}
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        return None
+
+    sustained, burst, hbm, kind = peaks()
+    ms_step = ms_max / args.steps
+    pf = pass_fwd_flop(b)
+    step_flop = 6 * pf
+    names = ["pass1_fwd", "pass2_fwd", "pass2_bwd", "pass1_bwd"]
+    flops = [pf, pf, 2 * pf, 2 * pf]
+    dom = max(range(4), key=lambda k: phases[k])
+    achieved = flops[dom] / (phases[dom] * 1e-3) / 1e12
+    return {
+        "metric": METRIC,
+        "value": b * N * world / (ms_step * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic N(0,1), seeded; inputs resident in HBM",
+        "config": {"workload": "order-2 causal poly-attention core fwd+bwd (config 2)", "global_batch": b * world,
+                   "heads": H, "seq_len": N, "dim_head": D, "parallelism": f"dp{world} (batch x head sharding)",
+                   "l2": "inputs (5 x 67 MB per GPU at batch 8) larger than L2; no flush"},
+        "tflops": step_flop / (ms_step * 1e-3) / 1e12,
+        "frac_of_peak": step_flop / (ms_step * 1e-3) / 1e12 / sustained,
+        "phases_ms": dict(zip(names, phases)),
+        "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": sustained,
+                     "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": None,
+                     "peak_kind": f"{kind} bf16 sustained"},
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu_baseline() if (world == 1 and not args.no_cpu) else None,
+    }
+
+
+def cpu_unit_seconds():
+    """Oracle (numpy, fp32) forward + backward of one (batch, head) unit of the workload."""
+    import numpy as np
+
+    from oracle import poly_oracle as O
+    r = np.random.default_rng(0)
+    a = [r.standard_normal((1, 1, N, D)).astype(np.float32) for _ in range(5)]
+    t0 = time.perf_counter()
+    O.order2_fwd(a[0], a[1], a[1], a[2], a[3], causal=True)
+    O.order2_bwd(a[0], a[1], a[1], a[2], a[3], a[4], causal=True)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline():
+    sec = cpu_unit_seconds()
+    # one unit = one head of one sequence; a token needs all H heads
+    return {"value": N / (sec * H), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one (batch, head) unit: seq {N}, dim_head {D}, fp32 numpy fwd+bwd, {sec:.2f} s"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    for _ in range(args.warmup):
+        cpu_unit_seconds()
+    sec = statistics.median(cpu_unit_seconds() for _ in range(args.steps))
+    v = N / (sec * H)
+    return {
+        "metric": METRIC, "impl": "reference", "value": v, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "order-2 causal poly-attention core fwd+bwd (config 2)", "global_batch": B,
+                   "heads": H, "seq_len": N, "dim_head": D, "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": "one (batch, head) unit per step, fp32 numpy restatement of the reference"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=B, help="per-GPU batch (smaller for profiling captures)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+    else:
+        if world > 1:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        res = run_ours(args, rank, world, local_rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

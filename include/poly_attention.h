@@ -163,6 +163,15 @@ POLY_API const char* poly_pass_bwd_kernel_name(const PolyPassBwdArgs* args);
 /* Last error message of the calling thread ("" if none). */
 POLY_API const char* poly_last_error(void);
 
+/* Number of kernels this library has launched in this process. */
+POLY_API unsigned long long poly_launch_count(void);
+
+/* Device error word of the current device (synchronous read): non-zero if a
+ * kernel's bounded wait gave up (1 = timeout) since the last reset. The
+ * kernel that gave up freed its resources and returned; its outputs are
+ * undefined. reset != 0 clears the word. */
+POLY_API int poly_device_error(int* out, int reset);
+
 /* ABI checks for bindings: POLY_ABI_VERSION and the struct sizes. */
 POLY_API int poly_abi_version(void);
 POLY_API size_t poly_sizeof_pass_args(void);

@@ -1,6 +1,7 @@
 // extern "C" boundary of libpolyattn.so: argument validation, kernel choice,
 // thread-local error reporting. Declarations and the reference interfaces
 // each entry point replaces are in include/poly_attention.h.
+#include <atomic>
 #include <cstdlib>
 #include <string>
 
@@ -11,6 +12,9 @@ namespace poly {
 static thread_local std::string g_error;
 
 void set_error(const std::string& msg) { g_error = msg; }
+
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 
 static int fail(int code, const std::string& msg) {
   set_error(msg);
@@ -57,6 +61,7 @@ using namespace poly;
 extern "C" {
 
 const char* poly_last_error(void) { return g_error.c_str(); }
+unsigned long long poly_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 int poly_abi_version(void) { return POLY_ABI_VERSION; }
 size_t poly_sizeof_pass_args(void) { return sizeof(PolyPassArgs); }
 size_t poly_sizeof_pass_bwd_args(void) { return sizeof(PolyPassBwdArgs); }

@@ -44,6 +44,9 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Thread-local error message for poly_last_error().
 void set_error(const std::string& msg);
 
+// Counts kernel launches made by this library (poly_launch_count()).
+void note_launch(int n = 1);
+
 inline int cuda_status(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return POLY_OK;
   set_error(std::string(what) + ": " + cudaGetErrorString(e));

@@ -41,6 +41,7 @@ int launch_lse_merge(const PolyMergeArgs& a, cudaStream_t s) {
     case POLY_F16: lse_merge_kernel<__half><<<grid, warps * 32, 0, s>>>(a); break;
     default: lse_merge_kernel<__nv_bfloat16><<<grid, warps * 32, 0, s>>>(a); break;
   }
+  note_launch();
   return cuda_status(cudaGetLastError(), "lse_merge launch");
 }
 

@@ -394,6 +394,7 @@ template <typename T, int DMAX>
 int launch_fwd_t(const PolyPassArgs& a, cudaStream_t s) {
   dim3 grid((a.seq_q + kWarps - 1) / kWarps, a.batch * a.heads);
   pass_fwd_simt_kernel<T, DMAX><<<grid, kWarps * 32, 0, s>>>(a);
+  note_launch(1);
   return cuda_status(cudaGetLastError(), "pass_fwd_simt launch");
 }
 
@@ -407,6 +408,7 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   pass_bwd_dq_simt_kernel<T, DMAX><<<gq, kWarps * 32, 0, s>>>(a, delta, fb_count);
   dim3 gk((a.fwd.seq_k + kWarps - 1) / kWarps, a.fwd.batch * a.fwd.kv_heads);
   pass_bwd_dkv_simt_kernel<T, DMAX><<<gk, kWarps * 32, 0, s>>>(a, delta, fb_count);
+  note_launch(3);
   return cuda_status(cudaGetLastError(), "pass_bwd_simt launch");
 }
 

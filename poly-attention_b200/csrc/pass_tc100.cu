@@ -101,7 +101,7 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return;
 }
 
-template <int D, typename T, bool HAS_BIAS>
+template <int D, typename T, bool HAS_BIAS, bool SOFTCLAMP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     pass_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
@@ -265,15 +265,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float* bt = sBias + (j & 1) * BN;
       const bool diag = p.causal && (j == mt);
       float tmax = -INFINITY;
+      if (SOFTCLAMP) {
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        float x = __uint_as_float(v[c]);
-        x = p.softclamp > 0.f ? tanhf(x * p.sc_in) * p.sc_out : x * p.sl2;
-        if (use_bias) x += bt[c];
-        if (diag && c > r) x = -INFINITY;
-        tmax = fmaxf(tmax, x);
-        v[c] = __float_as_uint(x);
+        for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(tanhf(__uint_as_float(v[c]) * p.sc_in) * p.sc_out);
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * p.sl2);
       }
+      if (use_bias) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) + bt[c]);
+      }
+      if (diag) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c)
+          if (c > r) v[c] = __float_as_uint(-INFINITY);
+      }
+#pragma unroll
+      for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, __uint_as_float(v[c]));
       const float m_new = fmaxf(m_run, tmax);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = ex2(m_run - m_use);
@@ -423,13 +432,13 @@ bool strides_ok(const int64_t* st, int n) {
   return true;
 }
 
-template <int D, typename T, bool HAS_BIAS>
+template <int D, typename T, bool HAS_BIAS, bool SOFTCLAMP>
 int launch_fwd_tc_t(const PolyPassArgs& a, cudaStream_t s) {
   using L = FwdLayout<D>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(pass_fwd_tc_kernel<D, T, HAS_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(pass_fwd_tc_kernel<D, T, HAS_BIAS, SOFTCLAMP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     L::kAlloc);
   });
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "cudaFuncSetAttribute(fwd tc)");
@@ -464,13 +473,16 @@ int launch_fwd_tc_t(const PolyPassArgs& a, cudaStream_t s) {
   p.epi_mul = a.epi_mul;
   p.epi_out = a.epi_out;
   dim3 grid(p.m_tiles, a.batch * a.heads);
-  pass_fwd_tc_kernel<D, T, HAS_BIAS><<<grid, kFwdThreads, L::kAlloc, s>>>(tq, tk, tv, p);
+  pass_fwd_tc_kernel<D, T, HAS_BIAS, SOFTCLAMP><<<grid, kFwdThreads, L::kAlloc, s>>>(tq, tk, tv, p);
+  note_launch(1);
   return cuda_status(cudaGetLastError(), "pass_fwd_tc launch");
 }
 
 template <int D, typename T>
 int fwd_bias(const PolyPassArgs& a, cudaStream_t s) {
-  return a.bias ? launch_fwd_tc_t<D, T, true>(a, s) : launch_fwd_tc_t<D, T, false>(a, s);
+  if (a.softclamp > 0.f)
+    return a.bias ? launch_fwd_tc_t<D, T, true, true>(a, s) : launch_fwd_tc_t<D, T, false, true>(a, s);
+  return a.bias ? launch_fwd_tc_t<D, T, true, false>(a, s) : launch_fwd_tc_t<D, T, false, false>(a, s);
 }
 
 }  // namespace
@@ -502,3 +514,12 @@ int launch_pass_bwd_tc(const PolyPassBwdArgs&, cudaStream_t) { return POLY_EUNSU
 size_t pass_bwd_tc_workspace(const PolyPassBwdArgs&) { return 0; }
 
 }  // namespace poly
+
+extern "C" POLY_API int poly_device_error(int* out, int reset) {
+  int rc = poly::cuda_status(cudaMemcpyFromSymbol(out, poly::g_poly_device_error, sizeof(int)), "read device error word");
+  if (rc == POLY_OK && reset) {
+    const int zero = 0;
+    rc = poly::cuda_status(cudaMemcpyToSymbol(poly::g_poly_device_error, &zero, sizeof(int)), "reset device error word");
+  }
+  return rc;
+}

@@ -69,6 +69,8 @@ EXPORTS = {
     "poly_pass_fwd_kernel_name": (ctypes.c_char_p, [ctypes.POINTER(PolyPassArgs)]),
     "poly_pass_bwd_kernel_name": (ctypes.c_char_p, [ctypes.POINTER(PolyPassBwdArgs)]),
     "poly_last_error": (ctypes.c_char_p, []),
+    "poly_launch_count": (ctypes.c_ulonglong, []),
+    "poly_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "poly_abi_version": (ctypes.c_int, []),
     "poly_sizeof_pass_args": (c_sz, []),
     "poly_sizeof_pass_bwd_args": (c_sz, []),
@@ -106,3 +108,15 @@ def check(rc: int, what: str):
     if rc == POLY_EUNSUPPORTED:
         raise NotImplementedError(msg)
     raise RuntimeError(msg)
+
+
+def launch_count() -> int:
+    """Kernels launched by libpolyattn.so in this process so far."""
+    return int(lib.poly_launch_count())
+
+
+def device_error(reset: bool = False) -> int:
+    """Device error word (non-zero: a bounded in-kernel wait gave up)."""
+    v = ctypes.c_int(0)
+    check(lib.poly_device_error(ctypes.byref(v), int(reset)), "poly_device_error")
+    return v.value
