@@ -1,0 +1,558 @@
+// tcgen05 / TMEM / TMA backward kernel for one poly-attention pass (sm_100a),
+// head_dim 64, bf16 / fp16. Replaces the Triton backward
+// (poly_attention/flash_poly_attention.py:164-316), without its dQ atomics
+// into the input dtype: dQ is reduced in fp32 and converted once.
+//
+// Key-stationary: one CTA owns 128 keys of one (batch, kv head) and walks
+// every 128-query tile (of every query head of its GQA group) that sees them.
+// Per query tile t:
+//   S^T  = K Q_t^T        (M=128 keys, N=128 queries, K=64)   -> TMEM
+//   dP^T = V dO_t^T                                          -> TMEM
+//   softmax warpgroup (thread = key row j):
+//     p = exp2(s*log2e*scale + bias_j - lse2_i), ds = p (dp - delta_i),
+//     dbias_j += ds (a register: the column sum of dS needs no reduction),
+//     P^T and dS^T (x softclamp factor) -> 128B-swizzled smem
+//   dV += P^T dO_t, dK += dS^T Q_t                         (TMEM accumulators)
+//   dQ_t = dS K  (A = the same dS^T tile read MN-major)    -> TMEM, double buffer
+//   dQ warpgroup: TMEM -> fp32 red.global.add into the dq accumulator
+// A preprocessing kernel forms delta_i = dout_i . out_i - dlse_i and the
+// log2-domain lse; a final kernel converts the fp32 dq accumulator.
+#include <mutex>
+#include <string>
+#include <type_traits>
+
+#include "common.cuh"
+#include "tc_host.cuh"
+#include "tc_ptx.cuh"
+
+namespace poly {
+
+extern __device__ int g_poly_device_error;
+
+namespace {
+using namespace tc;
+
+constexpr int D = 64;
+constexpr int BK = 128;   // keys per CTA
+constexpr int BQ = 128;   // queries per tile
+constexpr int kThreads = 384;
+
+struct BwdLayout {
+  static constexpr int kTile = 128 * D * 2;  // 16 KB: one [128][64] 16-bit tile
+  static constexpr int kK = 0;
+  static constexpr int kV = kK + kTile;
+  static constexpr int kQ = kV + kTile;          // 2 stages
+  static constexpr int kDO = kQ + 2 * kTile;     // 2 stages
+  static constexpr int kPT = kDO + 2 * kTile;    // [128 keys][128 queries]
+  static constexpr int kDST = kPT + 2 * kTile;
+  static constexpr int kLse = kDST + 2 * kTile;  // 2 stages x 128 floats
+  static constexpr int kDel = kLse + 2 * BQ * 4;
+  static constexpr int kBar = kDel + 2 * BQ * 4;
+  static constexpr int kNumBars = 16;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kBytes = kMisc + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 320, kDQ = 384;  // kDQ: 2 x 64
+};
+
+struct BwdParams {
+  int seq_q, seq_k, heads, kv_heads, nq_pad, q_tiles, causal;
+  float scale, sl2, sc_in, sc_out;
+  const float* bias; int64_t bias_stride[2];
+  float* dq_acc;                 // [b*heads][seq_q][64] fp32
+  const float* lse2;             // [b*heads][nq_pad] log2-domain lse (+inf padding)
+  const float* delta;            // [b*heads][nq_pad]
+  void* dk; int64_t dk_stride[3];
+  void* dv; int64_t dv_stride[3];
+  float* dbias; int64_t dbias_stride[2];
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t pk(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pk<__nv_bfloat16>(float a, float b) { return pack_bf16(a, b); }
+template <>
+__device__ __forceinline__ uint32_t pk<__half>(float a, float b) { return pack_f16(a, b); }
+
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > kWaitNs) return;
+}
+
+// Writes 32 consecutive 16-bit values (one 32-query chunk c of row r) into a
+// [128 rows][128 cols] tile stored as two 128-byte-swizzled 64-column atoms.
+__device__ __forceinline__ void store_chunk(uint8_t* tile, int r, int c, const uint32_t (&w)[16]) {
+  const int atom = c >> 1;
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) {
+    const int idx = (c & 1) * 4 + q4;
+    uint4 val = make_uint4(w[q4 * 4 + 0], w[q4 * 4 + 1], w[q4 * 4 + 2], w[q4 * 4 + 3]);
+    *reinterpret_cast<uint4*>(tile + atom * (128 * 128) + r * 128 + ((idx ^ (r & 7)) << 4)) = val;
+  }
+}
+
+template <typename T, bool SOFTCLAMP, bool HAS_BIAS>
+__global__ void __launch_bounds__(kThreads, 1)
+    pass_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                       const BwdParams p) {
+  using L = BwdLayout;
+  constexpr int kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sK = smem + L::kK;
+  uint8_t* sV = smem + L::kV;
+  uint8_t* sQ = smem + L::kQ;
+  uint8_t* sDO = smem + L::kDO;
+  uint8_t* sPT = smem + L::kPT;
+  uint8_t* sDST = smem + L::kDST;
+  float* sLse = (float*)(smem + L::kLse);
+  float* sDel = (float*)(smem + L::kDel);
+  uint64_t* bars = (uint64_t*)(smem + L::kBar);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;     // [2]
+  uint64_t* q_empty = bars + 3;    // [2]
+  uint64_t* sdp_full = bars + 5;
+  uint64_t* p_ready = bars + 6;
+  uint64_t* mma_done = bars + 7;
+  uint64_t* dq_full = bars + 8;    // [2]
+  uint64_t* dq_free = bars + 10;   // [2]
+  uint64_t* dkv_done = bars + 12;
+  uint64_t* drain = bars + 13;
+  uint32_t* tmem_slot = (uint32_t*)(smem + L::kMisc);
+  volatile int* abort_flag = (volatile int*)(smem + L::kMisc + 4);
+  int* err = &g_poly_device_error;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x;
+  const int b = blockIdx.y / p.kv_heads, kvh = blockIdx.y - b * p.kv_heads;
+  const int rep = p.heads / p.kv_heads;
+  const int qt0 = p.causal ? kt : 0;
+  const int nqt = max(0, p.q_tiles - qt0);
+  const int NT = rep * nqt;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+      mbar_init(&dq_full[s], 1);
+      mbar_init(&dq_free[s], 128);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(p_ready, 128);
+    mbar_init(mma_done, 1);
+    mbar_init(dkv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, L::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto tile_of = [&](int t, int& h, int& qt) {
+    const int hr = t / max(nqt, 1);
+    qt = qt0 + (t - hr * nqt);
+    h = kvh * rep + hr;
+  };
+
+  if (warp == 0) {
+    if (lane == 0 && NT > 0) {
+      // ------------------------------------------------ TMA producer
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_do);
+      mbar_arrive_expect_tx(kv_full, 2 * L::kTile);
+      tma_load_4d(sK, &tm_k, kv_full, 0, kt * BK, kvh, b);
+      tma_load_4d(sV, &tm_v, kv_full, 0, kt * BK, kvh, b);
+      int issued = 0;
+      for (int t = 0; t < NT; ++t) {
+        const int s = t & 1;
+        if (t >= 2 && !mbar_wait(&q_empty[s], ((t >> 1) - 1) & 1, abort_flag, err, 1)) break;
+        int h, qt;
+        tile_of(t, h, qt);
+        const int64_t row = (int64_t)(b * p.heads + h) * p.nq_pad + qt * BQ;
+        mbar_arrive_expect_tx(&q_full[s], 2 * L::kTile + 2 * BQ * 4);
+        tma_load_4d(sQ + s * L::kTile, &tm_q, &q_full[s], 0, qt * BQ, h, b);
+        tma_load_4d(sDO + s * L::kTile, &tm_do, &q_full[s], 0, qt * BQ, h, b);
+        bulk_load(sLse + s * BQ, p.lse2 + row, BQ * 4, &q_full[s]);
+        bulk_load(sDel + s * BQ, p.delta + row, BQ * 4, &q_full[s]);
+        issued = t + 1;
+      }
+      if (*abort_flag) {
+        drain_wait(kv_full, 0);
+        for (int t = max(0, issued - 2); t < issued; ++t) drain_wait(&q_full[t & 1], (t >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && NT > 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idSD = idesc_f16(128, 128, kIsBf16, 0, 0);   // K-major x K-major
+      constexpr uint32_t idKV = idesc_f16(128, D, kIsBf16, 0, 1);     // P^T / dS^T  x  dO / Q (MN)
+      constexpr uint32_t idQ = idesc_f16(128, D, kIsBf16, 1, 1);      // dS (MN view) x K (MN)
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), qa = smem_u32(sQ), doa = smem_u32(sDO);
+      const uint32_t pta = smem_u32(sPT), dsa = smem_u32(sDST);
+      auto issue_sdp = [&](int s) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          mma_f16_ss(tmem + L::kS, smem_desc_sw128(ka + kk * 32, 16, 1024),
+                     smem_desc_sw128(qa + s * L::kTile + kk * 32, 16, 1024), idSD, kk > 0);
+          mma_f16_ss(tmem + L::kDP, smem_desc_sw128(va + kk * 32, 16, 1024),
+                     smem_desc_sw128(doa + s * L::kTile + kk * 32, 16, 1024), idSD, kk > 0);
+        }
+        mma_commit(sdp_full);
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag, err, 2) && mbar_wait(&q_full[0], 0, abort_flag, err, 3);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0);
+      }
+      for (int t = 0; ok && t < NT; ++t) {
+        const int s = t & 1;
+        if (!mbar_wait(p_ready, t & 1, abort_flag, err, 4)) break;
+        tc_fence_after();
+        if (t + 1 < NT) {
+          if (!mbar_wait(&q_full[(t + 1) & 1], ((t + 1) >> 1) & 1, abort_flag, err, 5)) break;
+          tc_fence_after();
+          issue_sdp((t + 1) & 1);
+        }
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t aoff = (uint32_t)(kk >> 2) * (128 * 128) + (uint32_t)(kk & 3) * 32;
+          const uint32_t acc = (t > 0 || kk > 0);
+          mma_f16_ss(tmem + L::kDV, smem_desc_sw128(pta + aoff, 16, 1024),
+                     smem_desc_sw128(doa + s * L::kTile + kk * 2048, 128 * 128, 1024), idKV, acc);
+          mma_f16_ss(tmem + L::kDK, smem_desc_sw128(dsa + aoff, 16, 1024),
+                     smem_desc_sw128(qa + s * L::kTile + kk * 2048, 128 * 128, 1024), idKV, acc);
+        }
+        if (t >= 2 && !mbar_wait(&dq_free[s], ((t >> 1) - 1) & 1, abort_flag, err, 6)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          mma_f16_ss(tmem + L::kDQ + s * D, smem_desc_sw128(dsa + kk * 2048, 128 * 128, 1024),
+                     smem_desc_sw128(ka + kk * 2048, 128 * 128, 1024), idQ, kk > 0);
+        }
+        mma_commit(&q_empty[s]);
+        mma_commit(mma_done);
+        mma_commit(&dq_full[s]);
+      }
+      mma_commit(dkv_done);
+      mma_commit(drain);
+      drain_wait(drain, 0);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // -------------------------------------------------- softmax-backward (thread = key row)
+    const int r = (warp & 3) * 32 + lane;
+    const int j = kt * BK + r;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const bool key_ok = j < p.seq_k;
+    float b2 = 0.f;
+    if (HAS_BIAS && key_ok) {
+      const float braw = p.bias[b * p.bias_stride[0] + kvh * p.bias_stride[1] + j];
+      b2 = braw <= kDeadBias ? -INFINITY : braw * kLog2e;
+    }
+    float dbias = 0.f;
+    bool ok = true;
+    for (int t = 0; t < NT; ++t) {
+      const int s = t & 1;
+      int h, qt;
+      tile_of(t, h, qt);
+      if (!mbar_wait_warp(sdp_full, t & 1, abort_flag, err, 7)) { ok = false; break; }
+      if (t > 0 && !mbar_wait_warp(mma_done, (t - 1) & 1, abort_flag, err, 8)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = p.causal && qt == kt;
+      const float* lse = sLse + s * BQ;
+      const float* del = sDel + s * BQ;
+#pragma unroll 1
+      for (int c = 0; c < BQ / 32; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tmem + lane_base + L::kS + c * 32, sv);
+        tmem_ld32(tmem + lane_base + L::kDP + c * 32, dv);
+        tmem_wait_ld();
+        uint32_t pw[16], dw[16];
+#pragma unroll
+        for (int u = 0; u < 32; u += 2) {
+          float pp[2], dd[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int il = c * 32 + u + e;
+            const float sr = __uint_as_float(sv[u + e]);
+            float x, dfac = 1.f;
+            if (SOFTCLAMP) {
+              const float th = tanhf(sr * p.sc_in);
+              dfac = 1.f - th * th;
+              x = th * p.sc_out;
+            } else {
+              x = sr * p.sl2;
+            }
+            float pr = ex2(x + b2 - lse[il]);
+            if (!key_ok || (diag && il < r)) pr = 0.f;
+            const float ds = pr * (__uint_as_float(dv[u + e]) - del[il]);
+            dbias += ds;
+            pp[e] = pr;
+            dd[e] = SOFTCLAMP ? ds * dfac : ds;
+          }
+          pw[u >> 1] = pk<T>(pp[0], pp[1]);
+          dw[u >> 1] = pk<T>(dd[0], dd[1]);
+        }
+        store_chunk(sPT, r, c, pw);
+        store_chunk(sDST, r, c, dw);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_ready);
+    }
+    // dK, dV, dbias for this key row. tcgen05.ld is warp-collective: every
+    // lane runs it (warp-uniform condition); only the stores depend on key_ok.
+    bool have = ok && NT > 0 && mbar_wait_warp(dkv_done, 0, abort_flag, err, 9);
+    if (have) tc_fence_after();
+    if (have || NT == 0) {
+      T* dkp = (T*)p.dk + b * p.dk_stride[0] + kvh * p.dk_stride[1] + (int64_t)j * p.dk_stride[2];
+      T* dvp = (T*)p.dv + b * p.dv_stride[0] + kvh * p.dv_stride[1] + (int64_t)j * p.dv_stride[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t a[32], c2[32];
+        if (have) {
+          tmem_ld32(tmem + lane_base + L::kDK + half * 32, a);
+          tmem_ld32(tmem + lane_base + L::kDV + half * 32, c2);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int u = 0; u < 32; ++u) a[u] = c2[u] = 0u;
+        }
+        if (key_ok) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 wk, wv;
+            uint32_t* k4 = &wk.x;
+            uint32_t* v4 = &wv.x;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int u = q8 * 8 + 2 * e;
+              k4[e] = pk<T>(__uint_as_float(a[u]) * p.scale, __uint_as_float(a[u + 1]) * p.scale);
+              v4[e] = pk<T>(__uint_as_float(c2[u]), __uint_as_float(c2[u + 1]));
+            }
+            *reinterpret_cast<uint4*>(dkp + half * 32 + q8 * 8) = wk;
+            *reinterpret_cast<uint4*>(dvp + half * 32 + q8 * 8) = wv;
+          }
+        }
+      }
+      if (key_ok && p.dbias) p.dbias[b * p.dbias_stride[0] + kvh * p.dbias_stride[1] + j] = dbias;
+    }
+  } else if (warp >= 8) {
+    // -------------------------------------------------- dQ reduction (thread = query row)
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    for (int t = 0; t < NT; ++t) {
+      const int s = t & 1;
+      int h, qt;
+      tile_of(t, h, qt);
+      if (!mbar_wait_warp(&dq_full[s], (t >> 1) & 1, abort_flag, err, 10)) break;
+      tc_fence_after();
+      uint32_t a[32], c2[32];
+      tmem_ld32(tmem + lane_base + L::kDQ + s * D, a);
+      tmem_ld32(tmem + lane_base + L::kDQ + s * D + 32, c2);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&dq_free[s]);
+      const int i = qt * BQ + r;
+      if (i < p.seq_q) {
+        float* dst = p.dq_acc + ((int64_t)(b * p.heads + h) * p.seq_q + i) * D;
+#pragma unroll
+        for (int u = 0; u < 32; u += 4) {
+          red_add_v4(dst + u, __uint_as_float(a[u]), __uint_as_float(a[u + 1]), __uint_as_float(a[u + 2]),
+                     __uint_as_float(a[u + 3]));
+          red_add_v4(dst + 32 + u, __uint_as_float(c2[u]), __uint_as_float(c2[u + 1]), __uint_as_float(c2[u + 2]),
+                     __uint_as_float(c2[u + 3]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, L::kTmemCols);
+}
+
+// delta_i = dout_i . out_i - dlse_i and lse2_i = lse_i * log2(e), padded to
+// nq_pad rows per (batch, head) with (delta 0, lse2 +inf) so padded queries
+// get p = 0. One warp per row.
+template <typename T>
+__global__ void bwd_prep_kernel(const PolyPassBwdArgs a, float* lse2, float* delta, int nq_pad) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)a.fwd.batch * a.fwd.heads * nq_pad;
+  if (w >= rows) return;
+  const int i = (int)(w % nq_pad);
+  const int bh = (int)(w / nq_pad);
+  const int b = bh / a.fwd.heads, h = bh - b * a.fwd.heads;
+  if (i >= a.fwd.seq_q) {
+    if (lane == 0) {
+      lse2[w] = INFINITY;
+      delta[w] = 0.f;
+    }
+    return;
+  }
+  const T* o = (const T*)a.fwd.out + b * a.fwd.out_stride[0] + h * a.fwd.out_stride[1] + (int64_t)i * a.fwd.out_stride[2];
+  const T* g = (const T*)a.dout + b * a.dout_stride[0] + h * a.dout_stride[1] + (int64_t)i * a.dout_stride[2];
+  float s = 0.f;
+  for (int t = lane; t < D; t += 32) s += to_f32(o[t]) * to_f32(g[t]);
+  s = warp_sum(s);
+  if (lane == 0) {
+    if (a.dlse) s -= a.dlse[b * a.dlse_stride[0] + h * a.dlse_stride[1] + i];
+    delta[w] = s;
+    lse2[w] = a.fwd.lse[b * a.fwd.lse_stride[0] + h * a.fwd.lse_stride[1] + i] * kLog2e;
+  }
+}
+
+// dq = scale * dq_acc (+ dq when accumulating), 8 elements per thread.
+template <typename T>
+__global__ void bwd_dq_convert_kernel(const PolyPassBwdArgs a, const float* dq_acc) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)a.fwd.batch * a.fwd.heads * a.fwd.seq_q * (D / 8);
+  if (idx >= total) return;
+  const int c8 = (int)(idx % (D / 8));
+  const int64_t row = idx / (D / 8);
+  const int i = (int)(row % a.fwd.seq_q);
+  const int bh = (int)(row / a.fwd.seq_q);
+  const int b = bh / a.fwd.heads, h = bh - b * a.fwd.heads;
+  const float* src = dq_acc + row * D + c8 * 8;
+  T* dst = (T*)a.dq + b * a.dq_stride[0] + h * a.dq_stride[1] + (int64_t)i * a.dq_stride[2] + c8 * 8;
+  const float4 x0 = *reinterpret_cast<const float4*>(src);
+  const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+  float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  const float sc = a.fwd.scale;
+  if (a.dq_accumulate) {
+    const uint4 old = *reinterpret_cast<const uint4*>(dst);
+    const uint32_t* ow = &old.x;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const T* pr = reinterpret_cast<const T*>(&ow[e]);
+      v[2 * e] = v[2 * e] * sc + to_f32(pr[0]);
+      v[2 * e + 1] = v[2 * e + 1] * sc + to_f32(pr[1]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] *= sc;
+  }
+  uint4 out;
+  uint32_t* w = &out.x;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) w[e] = pk<T>(v[2 * e], v[2 * e + 1]);
+  *reinterpret_cast<uint4*>(dst) = out;
+}
+
+struct BwdWs {
+  float* dq_acc;
+  float* lse2;
+  float* delta;
+  int nq_pad;
+  size_t bytes;
+};
+
+BwdWs bwd_ws(const PolyPassBwdArgs& a) {
+  BwdWs w{};
+  w.nq_pad = (a.fwd.seq_q + BQ - 1) / BQ * BQ;
+  const size_t bh = (size_t)a.fwd.batch * a.fwd.heads;
+  const size_t acc = (bh * a.fwd.seq_q * D * 4 + 255) / 256 * 256;
+  const size_t vec = (bh * w.nq_pad * 4 + 255) / 256 * 256;
+  w.bytes = acc + 2 * vec;
+  char* base = (char*)a.workspace;
+  w.dq_acc = (float*)base;
+  w.lse2 = (float*)(base + acc);
+  w.delta = (float*)(base + acc + vec);
+  return w;
+}
+
+template <typename T, bool SOFTCLAMP, bool HAS_BIAS>
+int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
+  using L = BwdLayout;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+  });
+  if (attr_err != cudaSuccess) return cuda_status(attr_err, "cudaFuncSetAttribute(bwd tc)");
+  const PolyPassArgs& f = a.fwd;
+  BwdWs w = bwd_ws(a);
+  CUtensorMap tq, tdo, tk, tv;
+  int rc = make_map(&tq, f.q, f.dtype, D, f.seq_q, f.heads, f.batch, f.q_stride, BQ);
+  if (!rc) rc = make_map(&tdo, a.dout, f.dtype, D, f.seq_q, f.heads, f.batch, a.dout_stride, BQ);
+  if (!rc) rc = make_map(&tk, f.k, f.dtype, D, f.seq_k, f.kv_heads, f.batch, f.k_stride, BK);
+  if (!rc) rc = make_map(&tv, f.v, f.dtype, D, f.seq_k, f.kv_heads, f.batch, f.v_stride, BK);
+  if (rc) return rc;
+  rc = cuda_status(cudaMemsetAsync(w.dq_acc, 0, (size_t)f.batch * f.heads * f.seq_q * D * 4, s), "memset dq acc");
+  if (rc) return rc;
+  const int64_t prow = (int64_t)f.batch * f.heads * w.nq_pad;
+  bwd_prep_kernel<T><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(a, w.lse2, w.delta, w.nq_pad);
+  BwdParams p{};
+  p.seq_q = f.seq_q;
+  p.seq_k = f.seq_k;
+  p.heads = f.heads;
+  p.kv_heads = f.kv_heads;
+  p.nq_pad = w.nq_pad;
+  p.q_tiles = w.nq_pad / BQ;
+  p.causal = f.causal;
+  p.scale = f.scale;
+  p.sl2 = f.scale * kLog2e;
+  p.sc_in = f.softclamp > 0.f ? f.scale / f.softclamp : 0.f;
+  p.sc_out = f.softclamp * kLog2e;
+  p.bias = f.bias;
+  p.bias_stride[0] = f.bias_stride[0];
+  p.bias_stride[1] = f.bias_stride[1];
+  p.dq_acc = w.dq_acc;
+  p.lse2 = w.lse2;
+  p.delta = w.delta;
+  p.dk = a.dk;
+  p.dv = a.dv;
+  for (int i = 0; i < 3; ++i) {
+    p.dk_stride[i] = a.dk_stride[i];
+    p.dv_stride[i] = a.dv_stride[i];
+  }
+  p.dbias = a.dbias;
+  p.dbias_stride[0] = a.dbias_stride[0];
+  p.dbias_stride[1] = a.dbias_stride[1];
+  dim3 grid((f.seq_k + BK - 1) / BK, f.batch * f.kv_heads);
+  pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, p);
+  const int64_t cthreads = (int64_t)f.batch * f.heads * f.seq_q * (D / 8);
+  bwd_dq_convert_kernel<T><<<(unsigned)((cthreads + 255) / 256), 256, 0, s>>>(a, w.dq_acc);
+  note_launch(3);
+  return cuda_status(cudaGetLastError(), "pass_bwd_tc launch");
+}
+
+template <typename T>
+int bwd_dispatch(const PolyPassBwdArgs& a, cudaStream_t s) {
+  const bool sc = a.fwd.softclamp > 0.f, bias = a.fwd.bias != nullptr;
+  if (sc) return bias ? launch_bwd_t<T, true, true>(a, s) : launch_bwd_t<T, true, false>(a, s);
+  return bias ? launch_bwd_t<T, false, true>(a, s) : launch_bwd_t<T, false, false>(a, s);
+}
+
+}  // namespace
+
+bool pass_bwd_tc_eligible(const PolyPassBwdArgs& a) {
+  const PolyPassArgs& f = a.fwd;
+  if (f.dtype != POLY_BF16 && f.dtype != POLY_F16) return false;
+  if (f.head_dim != D) return false;
+  if (f.key_mask || f.query_mask || f.v_mul) return false;
+  if (!aligned16(f.q) || !aligned16(f.k) || !aligned16(f.v) || !aligned16(a.dout) || !aligned16(a.dq) ||
+      !aligned16(a.dk) || !aligned16(a.dv) || !aligned16(f.out))
+    return false;
+  if (!strides_ok(f.q_stride, 3) || !strides_ok(f.k_stride, 3) || !strides_ok(f.v_stride, 3) ||
+      !strides_ok(a.dout_stride, 3) || !strides_ok(a.dq_stride, 3) || !strides_ok(a.dk_stride, 3) ||
+      !strides_ok(a.dv_stride, 3))
+    return false;
+  return true;
+}
+
+size_t pass_bwd_tc_workspace(const PolyPassBwdArgs& a) { return bwd_ws(a).bytes; }
+
+int launch_pass_bwd_tc(const PolyPassBwdArgs& a, cudaStream_t s) {
+  return a.fwd.dtype == POLY_BF16 ? bwd_dispatch<__nv_bfloat16>(a, s) : bwd_dispatch<__half>(a, s);
+}
+
+}  // namespace poly

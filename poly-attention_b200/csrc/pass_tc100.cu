@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "tc_ptx.cuh"
+#include "tc_host.cuh"
 
 namespace poly {
 
@@ -97,8 +98,9 @@ __device__ __forceinline__ float2 unpack2<__half>(uint32_t u) {
 // Bounded wait that ignores the abort flag: used only to drain copies and
 // MMAs already in flight before the CTA exits.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t it = 0; it < (1u << 22); ++it)
-    if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > kWaitNs) return;
 }
 
 template <int D, typename T, bool HAS_BIAS, bool SOFTCLAMP>
@@ -172,7 +174,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       int issued = 0;
       for (int j = 0; j < nt; ++j) {
         const int s = j % S;
-        if (j >= S && !mbar_wait(&kv_empty[s], ((j / S) - 1) & 1, abort_flag, err)) break;
+        if (j >= S && !mbar_wait(&kv_empty[s], ((j / S) - 1) & 1, abort_flag, err, 21)) break;
         mbar_arrive_expect_tx(&k_full[s], L::kKVBytes);
         for (int c = 0; c < ND; ++c)
           tma_load_4d(sK + s * L::kKVBytes + c * BN * 128, &tm_k, &k_full[s], c * 64, j * BN, kvh, b);
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sP);
       auto issue_s = [&](int j) -> bool {
         const int s = j % S;
-        if (!mbar_wait(&k_full[s], (j / S) & 1, abort_flag, err)) return false;
+        if (!mbar_wait(&k_full[s], (j / S) & 1, abort_flag, err, 22)) return false;
         tc_fence_after();
         const uint32_t d_t = tmem + L::kTmemS + (uint32_t)(j & 1) * BN;
 #pragma unroll
@@ -209,12 +211,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mma_commit(&s_full[j & 1]);
         return true;
       };
-      if (mbar_wait(q_full, 0, abort_flag, err) && issue_s(0)) {
+      if (mbar_wait(q_full, 0, abort_flag, err, 23) && issue_s(0)) {
         for (int j = 0; j < nt; ++j) {
           if (j + 1 < nt && !issue_s(j + 1)) break;
-          if (!mbar_wait(p_full, j & 1, abort_flag, err)) break;
+          if (!mbar_wait(p_full, j & 1, abort_flag, err, 24)) break;
           const int s = j % S;
-          if (!mbar_wait(&v_full[s], (j / S) & 1, abort_flag, err)) break;
+          if (!mbar_wait(&v_full[s], (j / S) & 1, abort_flag, err, 25)) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
@@ -238,6 +240,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const float* bias = HAS_BIAS ? p.bias + b * p.bias_stride[0] + kvh * p.bias_stride[1] : nullptr;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    int nbias = 0;
     for (int j = 0; j < nt && ok; ++j) {
       const bool tail = (j == kt_total - 1) && (p.seq_k % BN) != 0;
       const bool use_bias = HAS_BIAS || tail;
@@ -251,18 +254,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             bv = braw <= kDeadBias ? -INFINITY : braw * kLog2e;
           }
         }
-        sBias[(j & 1) * BN + tid] = bv;
-        mbar_arrive(&bias_ready[j & 1]);
-        if (!mbar_wait(&bias_ready[j & 1], (j >> 1) & 1, abort_flag, err)) { ok = false; break; }
+        // bias tiles are counted separately: without a bias only the tail tile uses one
+        sBias[(nbias & 1) * BN + tid] = bv;
+        mbar_arrive(&bias_ready[nbias & 1]);
+        if (!mbar_wait_warp(&bias_ready[nbias & 1], (nbias >> 1) & 1, abort_flag, err, 26)) { ok = false; break; }
       }
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, err)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1, abort_flag, err, 27)) { ok = false; break; }
       tc_fence_after();
       uint32_t v[BN];
       const uint32_t s_addr = tmem + lane_base + L::kTmemS + (uint32_t)(j & 1) * BN;
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
       tmem_wait_ld();
-      const float* bt = sBias + (j & 1) * BN;
+      const float* bt = sBias + (nbias & 1) * BN;
+      if (use_bias) ++nbias;
       const bool diag = p.causal && (j == mt);
       float tmax = -INFINITY;
       if (SOFTCLAMP) {
@@ -297,7 +302,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       m_run = m_new;
       if (j > 0) {
         // PV_{j-1} must be complete before O is rescaled and P is overwritten
-        if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, err)) { ok = false; break; }
+        if (!mbar_wait_warp(o_done, (j - 1) & 1, abort_flag, err, 28)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha < 1.f)) {
           const uint32_t o_addr = tmem + lane_base + L::kTmemO;
@@ -328,7 +333,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(o_done, (nt - 1) & 1, abort_flag, err)) {
+    if (ok && mbar_wait_warp(o_done, (nt - 1) & 1, abort_flag, err, 29)) {
       tc_fence_after();
       const int row = row0 + r;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -380,57 +385,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // ---------------------------------------------------------------- host side
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  });
-  return fn;
-}
-
-// 4-D tiled map over a [batch, heads, rows, d] tensor with (b, h, row) element
-// strides; box = 64 features x box_rows rows, 128-byte swizzle.
-int make_map(CUtensorMap* m, const void* base, int dtype, int d, int rows, int heads, int batch,
-             const int64_t* st, int box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) {
-    set_error("cuTensorMapEncodeTiled is unavailable");
-    return POLY_ECUDA;
-  }
-  const cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)heads, (cuuint64_t)batch};
-  const cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
-  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
-  const cuuint32_t es[4] = {1, 1, 1, 1};
-  const CUresult r = fn(m, dtype == POLY_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
-                        const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
-    return POLY_ECUDA;
-  }
-  return POLY_OK;
-}
-
-bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
-
-// Strides usable by TMA / 16-byte vector access: positive multiples of 8
-// elements (16 bytes for 16-bit types).
-bool strides_ok(const int64_t* st, int n) {
-  for (int i = 0; i < n; ++i)
-    if (st[i] <= 0 || (st[i] & 7)) return false;
-  return true;
-}
 
 template <int D, typename T, bool HAS_BIAS, bool SOFTCLAMP>
 int launch_fwd_tc_t(const PolyPassArgs& a, cudaStream_t s) {
@@ -509,9 +463,6 @@ int launch_pass_fwd_tc(const PolyPassArgs& a, cudaStream_t s) {
   return a.head_dim == 64 ? fwd_bias<64, __half>(a, s) : fwd_bias<128, __half>(a, s);
 }
 
-bool pass_bwd_tc_eligible(const PolyPassBwdArgs&) { return false; }
-int launch_pass_bwd_tc(const PolyPassBwdArgs&, cudaStream_t) { return POLY_EUNSUPPORTED; }
-size_t pass_bwd_tc_workspace(const PolyPassBwdArgs&) { return 0; }
 
 }  // namespace poly
 

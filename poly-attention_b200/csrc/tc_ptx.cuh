@@ -9,11 +9,20 @@
 namespace poly {
 namespace tc {
 
-// Every spin-wait below gives up after this many polls. A wait that gives up
-// records kErrTimeout in the device error word and raises the CTA-local abort
-// flag, so every role leaves its loop and the CTA frees its TMEM and exits.
-constexpr uint32_t kSpinLimit = 1u << 26;
+// Every spin-wait below gives up after kWaitNs nanoseconds of wall time
+// (%globaltimer). A wait that gives up records where it was in the device
+// error word (kErrTimeout | site << 8, first writer wins) and raises the
+// CTA-local abort flag; every other wait in the grid that sees a non-zero
+// error word gives up at once. Each role then leaves its loop, the CTA frees
+// its TMEM and returns, and the host reads the word (poly_device_error).
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
 constexpr int kErrTimeout = 1;
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -49,16 +58,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait. Returns false (and raises *abort) on timeout or if another
-// role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
-  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+// Bounded wait. Returns false (and raises *abort) on timeout, or if another
+// role of this CTA or any CTA of the grid already gave up. `site` names the
+// barrier for the error word.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                          int site = 0) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 1023u) == 1023u && *abort) return false;
+    if ((it & 63u) == 0) {
+      if (*abort || (err && *(volatile int*)err)) {
+        *abort = 1;
+        return false;
+      }
+      if (globaltimer() - t0 > kWaitNs) {
+        *abort = 1;
+        if (err) atomicCAS(err, 0, kErrTimeout | (site << 8));
+        return false;
+      }
+    }
   }
-  *abort = 1;
-  if (err) atomicExch(err, kErrTimeout);
-  return false;
+}
+
+// Same, with a warp-uniform result: roles whose warps then run
+// warp-collective tcgen05.ld / st must never split a warp on a wait.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                               int site = 0) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, err, site));
 }
 
 // ---------------------------------------------------------------- TMA
@@ -73,6 +100,20 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, uin
       "[%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Vector fp32 reduction into global memory (16-byte aligned).
+__device__ __forceinline__ void red_add_v4(float* gaddr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gaddr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
 }
 
 // ---------------------------------------------------------------- fences

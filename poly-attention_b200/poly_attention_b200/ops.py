@@ -161,9 +161,15 @@ def kernel_names(q, k, v, *, causal=False, bias=None, key_mask=None, query_mask=
     """(forward, backward) kernel family the library picks for these inputs."""
     a = PolyPassBwdArgs()
     out = torch.empty_like(q)
+    lse = torch.empty(q.shape[:3], device=q.device, dtype=torch.float32)
     keep = []
-    _fill_pass(a.fwd, q, k, v, out, None, causal=causal, softclamp=None, scale=None, bias=bias, key_mask=key_mask,
+    _fill_pass(a.fwd, q, k, v, out, lse, causal=causal, softclamp=None, scale=None, bias=bias, key_mask=key_mask,
                query_mask=query_mask, epi_mul=None, epi_out=None, keep=keep)
+    g = [torch.empty_like(t, memory_format=torch.contiguous_format) for t in (q, q, k, v)]
+    a.dout, a.dout_stride = g[0].data_ptr(), (g[0].stride(0), g[0].stride(1), g[0].stride(2))
+    a.dq, a.dq_stride = g[1].data_ptr(), (g[1].stride(0), g[1].stride(1), g[1].stride(2))
+    a.dk, a.dk_stride = g[2].data_ptr(), (g[2].stride(0), g[2].stride(1), g[2].stride(2))
+    a.dv, a.dv_stride = g[3].data_ptr(), (g[3].stride(0), g[3].stride(1), g[3].stride(2))
     return (lib.poly_pass_fwd_kernel_name(ctypes.byref(a.fwd)).decode(),
             lib.poly_pass_bwd_kernel_name(ctypes.byref(a)).decode())
 

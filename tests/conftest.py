@@ -23,3 +23,18 @@ def golden():
         with np.load(os.path.join(GOLDEN, f"{name}.npz")) as z:
             return {k: z[k] for k in z.files}
     return load
+
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts(request):
+    """After every GPU test: no kernel's bounded wait may have given up."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from poly_attention_b200 import _lib
+    torch.cuda.synchronize()
+    err = _lib.device_error(reset=True)
+    assert err == 0, f"a kernel wait gave up: device error word {err:#x} (site {err >> 8})"

@@ -287,3 +287,69 @@ def test_tc_forward_selected_and_matches(d, causal, n):
         eo, el = O.pass_fwd(q, np.repeat(k, 2, 1), np.repeat(v, 2, 1), causal=causal, bias=np.repeat(bias, 2, 1))
         assert_close(out, eo, dtype, f"out {dtype}")
         assert_close(lse, el, dtype, f"lse {dtype}")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("n,g", [(300, 2), (1024, 4)])
+@pytest.mark.parametrize("softclamp", [None, 20.0])
+def test_tc_backward_selected_and_matches(causal, n, g, softclamp):
+    """bf16 / fp16 with d = 64 must run the tcgen05 backward; grads vs oracle."""
+    import poly_attention_b200 as P
+    b, h, d = 1, 4, 64
+    r = h // g
+    for dtype in (torch.bfloat16, torch.float16):
+        q = quant(rnd((b, h, n, d), 1), dtype)
+        k, v = (quant(rnd((b, g, n, d), s), dtype) for s in (2, 3))
+        do = quant(rnd((b, h, n, d), 4), dtype)
+        bias = rnd((b, g, n), 5)
+        dlse = rnd((b, h, n), 6)
+        qt, kt, vt = dev(q, dtype), dev(k, dtype), dev(v, dtype)
+        assert P.kernel_names(qt, kt, vt, causal=causal)[1] == "tc100"
+        out, lse = P.pass_fwd(qt, kt, vt, causal=causal, softclamp=softclamp, bias=dev(bias))
+        dq, dk, dv, db = P.pass_bwd(qt, kt, vt, out, lse, dev(do, dtype), causal=causal, softclamp=softclamp,
+                                    bias=dev(bias), dlse=dev(dlse), want_dbias=True)
+        edq, edk, edv, edb = O._pass_bwd(q, np.repeat(k, r, 1), np.repeat(v, r, 1), do, scale=d ** -0.5,
+                                         causal=causal, softclamp_value=softclamp, key_mask=None, query_mask=None,
+                                         bias=np.repeat(bias, r, 1), dlse=dlse)
+        group = lambda t: t.reshape(b, g, r, *t.shape[2:]).sum(2)  # noqa: E731
+        assert_close(dq, edq, dtype, f"dq {dtype}")
+        assert_close(dk, group(edk), dtype, f"dk {dtype}")
+        assert_close(dv, group(edv), dtype, f"dv {dtype}")
+        # dbias_j = sum_i p_ij (dp_ij - delta_i): delta_i = dout_i . out_i uses the
+        # 16-bit forward output (relative error ~2^-8), so the bound grows with the
+        # column mass sum_i p_ij of key j.
+        _, lse_ref = O.pass_fwd(q, np.repeat(k, r, 1), np.repeat(v, r, 1), causal=causal,
+                                softclamp_value=softclamp, bias=np.repeat(bias, r, 1))
+        s_ = np.einsum("bhid,bhjd->bhij", q, np.repeat(k, r, 1)) * d ** -0.5
+        if softclamp:
+            s_ = softclamp * np.tanh(s_ / softclamp)
+        s_ = s_ + np.repeat(bias, r, 1)[..., None, :]
+        if causal:
+            s_ = np.where(np.triu(np.ones((n, n), bool), 1), -np.inf, s_)
+        mass = group(np.exp(s_ - lse_ref[..., None]).sum(-2))
+        err = np.abs(host(db) - group(edb))
+        bound = BF16_ATOL + BF16_RTOL * np.abs(group(edb)) + 4e-3 * mass
+        assert np.all(err <= bound), f"dbias {dtype}: worst excess {float((err - bound).max())}"
+
+
+@pytest.mark.parametrize("nq,nk", [(384, 300), (128, 200), (300, 384), (257, 129)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_tc_ragged_without_bias(nq, nk, causal):
+    """Ragged key tails without a bias take the kernels' tail-masking path."""
+    import poly_attention_b200 as P
+    dtype = torch.bfloat16
+    q = quant(rnd((1, 2, nq, 64), 1), dtype)
+    k, v = (quant(rnd((1, 2, nk, 64), s), dtype) for s in (2, 3))
+    do = quant(rnd((1, 2, nq, 64), 4), dtype)
+    qt, kt, vt = dev(q, dtype), dev(k, dtype), dev(v, dtype)
+    assert P.kernel_names(qt, kt, vt, causal=causal) == ("tc100", "tc100")
+    out, lse = P.pass_fwd(qt, kt, vt, causal=causal)
+    eo, el = O.pass_fwd(q, k, v, causal=causal)
+    assert_close(out, eo, dtype, "out")
+    assert_close(lse, el, dtype, "lse")
+    dq, dk, dv, _ = P.pass_bwd(qt, kt, vt, out, lse, dev(do, dtype), causal=causal)
+    e = O._pass_bwd(q, k, v, do, scale=0.125, causal=causal, softclamp_value=None, key_mask=None, query_mask=None,
+                    bias=None)
+    assert_close(dq, e[0], dtype, "dq")
+    assert_close(dk, e[1], dtype, "dk")
+    assert_close(dv, e[2], dtype, "dv")
