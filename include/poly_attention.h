@@ -155,6 +155,19 @@ POLY_API size_t poly_pass_bwd_workspace_size(const PolyPassBwdArgs* args);
 
 POLY_API int poly_lse_merge(const PolyMergeArgs* args, void* stream);
 
+/*
+ * poly_pass_bwd without a caller workspace. No counterpart in the reference:
+ * it exists for callers that cannot allocate device memory (FFI hosts that
+ * only pass existing buffers, processes whose device memory another
+ * allocator has fully planned). Scratch comes from an 8 MiB array built into
+ * the library (held per GPU until exit); larger problems get POLY_EINVAL.
+ * All calls on a device share that array: calls overlapping on the GPU race.
+ * The first call on a device resolves the array's address; make it before
+ * any stream capture. args->workspace is ignored.
+ */
+POLY_API int poly_pass_bwd_noalloc(const PolyPassBwdArgs* args, void* stream);
+POLY_API size_t poly_noalloc_scratch_bytes(void);
+
 /* Name of the kernel family poly_pass_fwd / poly_pass_bwd would launch for
  * these arguments ("tc100" tcgen05 path, "simt" CUDA-core path, "decode"). */
 POLY_API const char* poly_pass_fwd_kernel_name(const PolyPassArgs* args);

@@ -66,6 +66,8 @@ EXPORTS = {
     "poly_pass_bwd": (ctypes.c_int, [ctypes.POINTER(PolyPassBwdArgs), c_vp]),
     "poly_pass_bwd_workspace_size": (c_sz, [ctypes.POINTER(PolyPassBwdArgs)]),
     "poly_lse_merge": (ctypes.c_int, [ctypes.POINTER(PolyMergeArgs), c_vp]),
+    "poly_pass_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(PolyPassBwdArgs), c_vp]),
+    "poly_noalloc_scratch_bytes": (c_sz, []),
     "poly_pass_fwd_kernel_name": (ctypes.c_char_p, [ctypes.POINTER(PolyPassArgs)]),
     "poly_pass_bwd_kernel_name": (ctypes.c_char_p, [ctypes.POINTER(PolyPassBwdArgs)]),
     "poly_last_error": (ctypes.c_char_p, []),

@@ -1,0 +1,74 @@
+"""The allocation-free backward entry point, called through the C ABI.
+
+poly_pass_bwd_noalloc serves callers that cannot allocate device memory
+(an FFI host that only passes existing buffers, or a process whose device
+memory another allocator has fully planned): it draws its scratch from an
+array built into the library. Its results must match poly_pass_bwd, which
+uses a caller-provided workspace, on consecutive calls (the shared array
+keeps the previous call's contents, which must not leak into results).
+
+Named so pytest collects it last.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def _args(q, k, v, out, lse, do, dq, dk, dv, dbias, causal):
+    from poly_attention_b200 import _lib, ops
+    a = _lib.PolyPassBwdArgs()
+    keep = []
+    ops._fill_pass(a.fwd, q, k, v, out, lse, causal=causal, softclamp=None, scale=None, bias=None, key_mask=None,
+                   query_mask=None, epi_mul=None, epi_out=None, keep=keep)
+    for name, t in (("dout", do), ("dq", dq), ("dk", dk), ("dv", dv)):
+        setattr(a, name, t.data_ptr())
+        setattr(a, name + "_stride", (t.stride(0), t.stride(1), t.stride(2)))
+    a.dbias, a.dbias_stride = dbias.data_ptr(), (dbias.stride(0), dbias.stride(1))
+    return a, keep
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_noalloc_backward_matches_workspace_backward(causal):
+    import poly_attention_b200 as P
+    from poly_attention_b200 import _lib
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    torch.manual_seed(7)
+    for call in range(2):
+        b, h, g, n = 1, 4, 2, 384 + 64 * call
+        q = torch.randn(b, h, n, 64, device="cuda", dtype=torch.bfloat16)
+        k = torch.randn(b, g, n, 64, device="cuda", dtype=torch.bfloat16)
+        v = torch.randn(b, g, n, 64, device="cuda", dtype=torch.bfloat16)
+        do = torch.randn_like(q)
+        out, lse = P.pass_fwd(q, k, v, causal=causal)
+        ref = P.pass_bwd(q, k, v, out, lse, do, causal=causal, want_dbias=True)
+        got = [torch.full_like(ref[0], float("nan")), torch.full_like(ref[1], float("nan")),
+               torch.full_like(ref[2], float("nan")), torch.full_like(ref[3], float("nan"))]
+        a, keep = _args(q, k, v, out, lse, do, *got, causal)
+        need = _lib.lib.poly_pass_bwd_workspace_size(ctypes.byref(a))
+        assert 0 < need <= _lib.lib.poly_noalloc_scratch_bytes()
+        _lib.check(_lib.lib.poly_pass_bwd_noalloc(ctypes.byref(a), stream), "poly_pass_bwd_noalloc")
+        torch.cuda.synchronize()
+        for r_, g_ in zip(ref, got):
+            np.testing.assert_allclose(g_.float().cpu().numpy(), r_.float().cpu().numpy(), atol=ATOL, rtol=RTOL)
+        del keep
+
+
+def test_noalloc_rejects_oversized_problem():
+    import poly_attention_b200 as P
+    from poly_attention_b200 import _lib
+    b, h, n = 1, 16, 4096            # dq accumulator alone is 16 MiB > the built-in scratch
+    q = torch.randn(b, h, n, 64, device="cuda", dtype=torch.bfloat16)
+    out, lse = torch.empty_like(q), torch.zeros(b, h, n, device="cuda")
+    g = [torch.empty_like(q) for _ in range(4)]
+    db = torch.empty(b, h, n, device="cuda")
+    a, keep = _args(q, q, q, out, lse, g[0], g[1], g[2], g[3], db, True)
+    rc = _lib.lib.poly_pass_bwd_noalloc(ctypes.byref(a), None)
+    assert rc == _lib.POLY_EINVAL
+    assert "scratch" in _lib.lib.poly_last_error().decode()
+    del keep
