@@ -50,7 +50,7 @@ def build(verbose=False, debug=False, ptxas_v=False):
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
-        if r.returncode != 0 or ptxas_v:
+        if r.returncode != 0 or ptxas_v or "warning" in r.stderr:
             sys.stderr.write(r.stdout + r.stderr)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {cmd[-3]}")

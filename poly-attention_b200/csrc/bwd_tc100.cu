@@ -27,7 +27,17 @@
 
 namespace poly {
 
-extern __device__ int g_poly_device_error;
+// Device error word of this file's kernels (see read_device_error_bwd).
+static __device__ int g_poly_device_error = 0;
+
+int read_device_error_bwd(int* out, bool reset) {
+  int rc = cuda_status(cudaMemcpyFromSymbol(out, g_poly_device_error, sizeof(int)), "read device error word");
+  if (rc == POLY_OK && reset) {
+    const int zero = 0;
+    rc = cuda_status(cudaMemcpyToSymbol(g_poly_device_error, &zero, sizeof(int)), "reset device error word");
+  }
+  return rc;
+}
 
 namespace {
 using namespace tc;
@@ -35,7 +45,7 @@ using namespace tc;
 constexpr int D = 64;
 constexpr int BK = 128;   // keys per CTA
 constexpr int BQ = 128;   // queries per tile
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
 
 struct BwdLayout {
   static constexpr int kTile = 128 * D * 2;  // 16 KB: one [128][64] 16-bit tile
@@ -47,7 +57,8 @@ struct BwdLayout {
   static constexpr int kDST = kPT + 2 * kTile;
   static constexpr int kLse = kDST + 2 * kTile;  // 2 stages x 128 floats
   static constexpr int kDel = kLse + 2 * BQ * 4;
-  static constexpr int kBar = kDel + 2 * BQ * 4;
+  static constexpr int kDb = kDel + 2 * BQ * 4;   // d-bias partials of warpgroup 1
+  static constexpr int kBar = kDb + BK * 4;
   static constexpr int kNumBars = 16;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
@@ -110,6 +121,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sDST = smem + L::kDST;
   float* sLse = (float*)(smem + L::kLse);
   float* sDel = (float*)(smem + L::kDel);
+  float* sDb = (float*)(smem + L::kDb);
+  float dbias_part = 0.f;
   uint64_t* bars = (uint64_t*)(smem + L::kBar);
   uint64_t* kv_full = bars + 0;
   uint64_t* q_full = bars + 1;     // [2]
@@ -142,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&dq_free[s], 128);
     }
     mbar_init(sdp_full, 1);
-    mbar_init(p_ready, 128);
+    mbar_init(p_ready, 256);
     mbar_init(mma_done, 1);
     mbar_init(dkv_done, 1);
     mbar_init(drain, 1);
@@ -244,8 +257,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(drain);
       drain_wait(drain, 0);
     }
-  } else if (warp >= 4 && warp < 8) {
-    // -------------------------------------------------- softmax-backward (thread = key row)
+  } else if (warp >= 4 && warp < 12) {
+    // -------------------------------------------------- softmax-backward
+    // Two warpgroups: thread = key row r, warpgroup hw takes query columns
+    // [64 hw, 64 hw + 64) of every tile.
+    const int hw = (warp - 4) >> 2;
     const int r = (warp & 3) * 32 + lane;
     const int j = kt * BK + r;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
@@ -257,30 +273,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     float dbias = 0.f;
     bool ok = true;
-    for (int t = 0; t < NT; ++t) {
+    for (int t = 0; t < NT && ok; ++t) {
       const int s = t & 1;
       int h, qt;
       tile_of(t, h, qt);
       if (!mbar_wait_warp(sdp_full, t & 1, abort_flag, err, 7)) { ok = false; break; }
-      if (t > 0 && !mbar_wait_warp(mma_done, (t - 1) & 1, abort_flag, err, 8)) { ok = false; break; }
       tc_fence_after();
       const bool diag = p.causal && qt == kt;
-      const float* lse = sLse + s * BQ;
-      const float* del = sDel + s * BQ;
 #pragma unroll 1
-      for (int c = 0; c < BQ / 32; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = hw * 2 + cc;
         uint32_t sv[32], dv[32];
         tmem_ld32(tmem + lane_base + L::kS + c * 32, sv);
         tmem_ld32(tmem + lane_base + L::kDP + c * 32, dv);
         tmem_wait_ld();
+        const float4* l4 = reinterpret_cast<const float4*>(sLse + s * BQ + c * 32);
+        const float4* d4 = reinterpret_cast<const float4*>(sDel + s * BQ + c * 32);
         uint32_t pw[16], dw[16];
 #pragma unroll
-        for (int u = 0; u < 32; u += 2) {
-          float pp[2], dd[2];
+        for (int q = 0; q < 8; ++q) {
+          const float4 lq = l4[q], dq = d4[q];
+          const float lv[4] = {lq.x, lq.y, lq.z, lq.w};
+          const float dl[4] = {dq.x, dq.y, dq.z, dq.w};
+          float pp[4], dd[4];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int il = c * 32 + u + e;
-            const float sr = __uint_as_float(sv[u + e]);
+          for (int e = 0; e < 4; ++e) {
+            const int u = q * 4 + e;
+            const int il = c * 32 + u;
+            const float sr = __uint_as_float(sv[u]);
             float x, dfac = 1.f;
             if (SOFTCLAMP) {
               const float th = tanhf(sr * p.sc_in);
@@ -289,61 +309,68 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               x = sr * p.sl2;
             }
-            float pr = ex2(x + b2 - lse[il]);
+            float pr = ex2(x + (b2 - lv[e]));
             if (!key_ok || (diag && il < r)) pr = 0.f;
-            const float ds = pr * (__uint_as_float(dv[u + e]) - del[il]);
+            const float ds = pr * (__uint_as_float(dv[u]) - dl[e]);
             dbias += ds;
             pp[e] = pr;
             dd[e] = SOFTCLAMP ? ds * dfac : ds;
           }
-          pw[u >> 1] = pk<T>(pp[0], pp[1]);
-          dw[u >> 1] = pk<T>(dd[0], dd[1]);
+          pw[2 * q] = pk<T>(pp[0], pp[1]);
+          pw[2 * q + 1] = pk<T>(pp[2], pp[3]);
+          dw[2 * q] = pk<T>(dd[0], dd[1]);
+          dw[2 * q + 1] = pk<T>(dd[2], dd[3]);
+        }
+        // P^T / dS^T smem is free once the previous tile's MMAs completed
+        if (cc == 0 && t > 0 && !mbar_wait_warp(mma_done, (t - 1) & 1, abort_flag, err, 8)) {
+          ok = false;
+          break;
         }
         store_chunk(sPT, r, c, pw);
         store_chunk(sDST, r, c, dw);
       }
+      if (!ok) break;
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_ready);
     }
-    // dK, dV, dbias for this key row. tcgen05.ld is warp-collective: every
-    // lane runs it (warp-uniform condition); only the stores depend on key_ok.
+    // dK (warpgroup 0) or dV (warpgroup 1) for this key row. tcgen05.ld is
+    // warp-collective: every lane runs it; only the stores depend on key_ok.
     bool have = ok && NT > 0 && mbar_wait_warp(dkv_done, 0, abort_flag, err, 9);
     if (have) tc_fence_after();
     if (have || NT == 0) {
-      T* dkp = (T*)p.dk + b * p.dk_stride[0] + kvh * p.dk_stride[1] + (int64_t)j * p.dk_stride[2];
-      T* dvp = (T*)p.dv + b * p.dv_stride[0] + kvh * p.dv_stride[1] + (int64_t)j * p.dv_stride[2];
+      T* dst = hw == 0 ? (T*)p.dk + b * p.dk_stride[0] + kvh * p.dk_stride[1] + (int64_t)j * p.dk_stride[2]
+                       : (T*)p.dv + b * p.dv_stride[0] + kvh * p.dv_stride[1] + (int64_t)j * p.dv_stride[2];
+      const float mul = hw == 0 ? p.scale : 1.f;
+      const uint32_t col = hw == 0 ? L::kDK : L::kDV;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint32_t a[32], c2[32];
+        uint32_t a[32];
         if (have) {
-          tmem_ld32(tmem + lane_base + L::kDK + half * 32, a);
-          tmem_ld32(tmem + lane_base + L::kDV + half * 32, c2);
+          tmem_ld32(tmem + lane_base + col + half * 32, a);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int u = 0; u < 32; ++u) a[u] = c2[u] = 0u;
+          for (int u = 0; u < 32; ++u) a[u] = 0u;
         }
         if (key_ok) {
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8) {
-            uint4 wk, wv;
-            uint32_t* k4 = &wk.x;
-            uint32_t* v4 = &wv.x;
+            uint4 w4;
+            uint32_t* wp = &w4.x;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int u = q8 * 8 + 2 * e;
-              k4[e] = pk<T>(__uint_as_float(a[u]) * p.scale, __uint_as_float(a[u + 1]) * p.scale);
-              v4[e] = pk<T>(__uint_as_float(c2[u]), __uint_as_float(c2[u + 1]));
+              wp[e] = pk<T>(__uint_as_float(a[u]) * mul, __uint_as_float(a[u + 1]) * mul);
             }
-            *reinterpret_cast<uint4*>(dkp + half * 32 + q8 * 8) = wk;
-            *reinterpret_cast<uint4*>(dvp + half * 32 + q8 * 8) = wv;
+            *reinterpret_cast<uint4*>(dst + half * 32 + q8 * 8) = w4;
           }
         }
       }
-      if (key_ok && p.dbias) p.dbias[b * p.dbias_stride[0] + kvh * p.dbias_stride[1] + j] = dbias;
     }
-  } else if (warp >= 8) {
+    if (hw == 1) sDb[r] = dbias;
+    dbias_part = dbias;
+  } else if (warp >= 12) {
     // -------------------------------------------------- dQ reduction (thread = query row)
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
@@ -376,36 +403,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, L::kTmemCols);
+  // d-bias = sum of both warpgroups' partial column sums
+  if (warp >= 4 && warp < 8 && p.dbias) {
+    const int r = (warp & 3) * 32 + lane;
+    const int j = kt * BK + r;
+    if (j < p.seq_k) p.dbias[b * p.dbias_stride[0] + kvh * p.dbias_stride[1] + j] = dbias_part + sDb[r];
+  }
 }
 
 // delta_i = dout_i . out_i - dlse_i and lse2_i = lse_i * log2(e), padded to
 // nq_pad rows per (batch, head) with (delta 0, lse2 +inf) so padded queries
-// get p = 0. One warp per row.
+// get p = 0. Eight lanes per row, 16-byte loads.
 template <typename T>
 __global__ void bwd_prep_kernel(const PolyPassBwdArgs a, float* lse2, float* delta, int nq_pad) {
-  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  const int sub = threadIdx.x & 7;
   const int64_t rows = (int64_t)a.fwd.batch * a.fwd.heads * nq_pad;
   if (w >= rows) return;
   const int i = (int)(w % nq_pad);
   const int bh = (int)(w / nq_pad);
   const int b = bh / a.fwd.heads, h = bh - b * a.fwd.heads;
-  if (i >= a.fwd.seq_q) {
-    if (lane == 0) {
+  float s = 0.f;
+  if (i < a.fwd.seq_q) {
+    const T* o = (const T*)a.fwd.out + b * a.fwd.out_stride[0] + h * a.fwd.out_stride[1] +
+                 (int64_t)i * a.fwd.out_stride[2] + sub * 8;
+    const T* g = (const T*)a.dout + b * a.dout_stride[0] + h * a.dout_stride[1] + (int64_t)i * a.dout_stride[2] +
+                 sub * 8;
+    const uint4 ov = *reinterpret_cast<const uint4*>(o);
+    const uint4 gv = *reinterpret_cast<const uint4*>(g);
+    const T* op = reinterpret_cast<const T*>(&ov);
+    const T* gp = reinterpret_cast<const T*>(&gv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s += to_f32(op[e]) * to_f32(gp[e]);
+  }
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  s += __shfl_xor_sync(0xffffffffu, s, 4);
+  if (sub == 0) {
+    if (i >= a.fwd.seq_q) {
       lse2[w] = INFINITY;
       delta[w] = 0.f;
+    } else {
+      if (a.dlse) s -= a.dlse[b * a.dlse_stride[0] + h * a.dlse_stride[1] + i];
+      delta[w] = s;
+      lse2[w] = a.fwd.lse[b * a.fwd.lse_stride[0] + h * a.fwd.lse_stride[1] + i] * kLog2e;
     }
-    return;
-  }
-  const T* o = (const T*)a.fwd.out + b * a.fwd.out_stride[0] + h * a.fwd.out_stride[1] + (int64_t)i * a.fwd.out_stride[2];
-  const T* g = (const T*)a.dout + b * a.dout_stride[0] + h * a.dout_stride[1] + (int64_t)i * a.dout_stride[2];
-  float s = 0.f;
-  for (int t = lane; t < D; t += 32) s += to_f32(o[t]) * to_f32(g[t]);
-  s = warp_sum(s);
-  if (lane == 0) {
-    if (a.dlse) s -= a.dlse[b * a.dlse_stride[0] + h * a.dlse_stride[1] + i];
-    delta[w] = s;
-    lse2[w] = a.fwd.lse[b * a.fwd.lse_stride[0] + h * a.fwd.lse_stride[1] + i] * kLog2e;
   }
 }
 
@@ -489,7 +531,7 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   rc = cuda_status(cudaMemsetAsync(w.dq_acc, 0, (size_t)f.batch * f.heads * f.seq_q * D * 4, s), "memset dq acc");
   if (rc) return rc;
   const int64_t prow = (int64_t)f.batch * f.heads * w.nq_pad;
-  bwd_prep_kernel<T><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(a, w.lse2, w.delta, w.nq_pad);
+  bwd_prep_kernel<T><<<(unsigned)((prow * 8 + 255) / 256), 256, 0, s>>>(a, w.lse2, w.delta, w.nq_pad);
   BwdParams p{};
   p.seq_q = f.seq_q;
   p.seq_k = f.seq_k;

@@ -62,6 +62,15 @@ extern "C" {
 
 const char* poly_last_error(void) { return g_error.c_str(); }
 unsigned long long poly_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int poly_device_error(int* out, int reset) {
+  if (!out) return fail(POLY_EINVAL, "null out");
+  int a = 0, b = 0;
+  int rc = read_device_error_fwd(&a, reset != 0);
+  if (!rc) rc = read_device_error_bwd(&b, reset != 0);
+  *out = a ? a : b;
+  return rc;
+}
 int poly_abi_version(void) { return POLY_ABI_VERSION; }
 size_t poly_sizeof_pass_args(void) { return sizeof(PolyPassArgs); }
 size_t poly_sizeof_pass_bwd_args(void) { return sizeof(PolyPassBwdArgs); }

@@ -66,6 +66,9 @@ bool pass_bwd_tc_eligible(const PolyPassBwdArgs& a);
 int launch_pass_bwd_tc(const PolyPassBwdArgs& a, cudaStream_t s);
 size_t pass_bwd_tc_workspace(const PolyPassBwdArgs& a);
 
+int read_device_error_fwd(int* out, bool reset);
+int read_device_error_bwd(int* out, bool reset);
+
 bool pass_decode_eligible(const PolyPassArgs& a);
 int launch_pass_decode(const PolyPassArgs& a, cudaStream_t s);
 size_t pass_decode_workspace(const PolyPassArgs& a);

@@ -27,8 +27,19 @@
 
 namespace poly {
 
-// Device error word: set by bounded waits that gave up (kErrTimeout).
-__device__ int g_poly_device_error = 0;
+// Device error word of this file's kernels: set by bounded waits that gave up.
+// (Without relocatable device code every .cu file has its own; the host
+// combines them in poly_device_error.)
+static __device__ int g_poly_device_error = 0;
+
+int read_device_error_fwd(int* out, bool reset) {
+  int rc = cuda_status(cudaMemcpyFromSymbol(out, g_poly_device_error, sizeof(int)), "read device error word");
+  if (rc == POLY_OK && reset) {
+    const int zero = 0;
+    rc = cuda_status(cudaMemcpyToSymbol(g_poly_device_error, &zero, sizeof(int)), "reset device error word");
+  }
+  return rc;
+}
 
 namespace {
 using namespace tc;
@@ -70,12 +81,6 @@ struct FwdParams {
   const void* epi_mul; int64_t epi_mul_stride[3];
   void* epi_out; int64_t epi_out_stride[3];
 };
-
-__device__ __forceinline__ float tanh_approx(float x) {
-  float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -465,12 +470,3 @@ int launch_pass_fwd_tc(const PolyPassArgs& a, cudaStream_t s) {
 
 
 }  // namespace poly
-
-extern "C" POLY_API int poly_device_error(int* out, int reset) {
-  int rc = poly::cuda_status(cudaMemcpyFromSymbol(out, poly::g_poly_device_error, sizeof(int)), "read device error word");
-  if (rc == POLY_OK && reset) {
-    const int zero = 0;
-    rc = poly::cuda_status(cudaMemcpyToSymbol(poly::g_poly_device_error, &zero, sizeof(int)), "reset device error word");
-  }
-  return rc;
-}
