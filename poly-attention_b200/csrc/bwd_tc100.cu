@@ -55,7 +55,8 @@ struct BwdLayout {
   static constexpr int kDO = kQ + 2 * kTile;     // 2 stages
   static constexpr int kPT = kDO + 2 * kTile;    // [128 keys][128 queries]
   static constexpr int kDST = kPT + 2 * kTile;
-  static constexpr int kLse = kDST + 2 * kTile;  // 2 stages x 128 floats
+  static constexpr int kDQS = kDST + 2 * kTile;  // dQ staging: 2 x [128 rows][32 fp32], swizzled
+  static constexpr int kLse = kDQS + 2 * kTile;  // 2 stages x 128 floats
   static constexpr int kDel = kLse + 2 * BQ * 4;
   static constexpr int kDb = kDel + 2 * BQ * 4;   // d-bias partials of warpgroup 1
   static constexpr int kBar = kDb + BK * 4;
@@ -108,7 +109,7 @@ template <typename T, bool SOFTCLAMP, bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1)
     pass_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                       const BwdParams p) {
+                       const __grid_constant__ CUtensorMap tm_dq, const BwdParams p) {
   using L = BwdLayout;
   constexpr int kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   extern __shared__ uint8_t smem_raw[];
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sDO = smem + L::kDO;
   uint8_t* sPT = smem + L::kPT;
   uint8_t* sDST = smem + L::kDST;
+  uint8_t* sDQ = smem + L::kDQS;
   float* sLse = (float*)(smem + L::kLse);
   float* sDel = (float*)(smem + L::kDel);
   float* sDb = (float*)(smem + L::kDb);
@@ -378,7 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = t & 1;
       int h, qt;
       tile_of(t, h, qt);
-      if (!mbar_wait_warp(&dq_full[s], (t >> 1) & 1, abort_flag, err, 10)) break;
+      // exit decision shared by the whole warpgroup (it meets at named barriers)
+      if (!named_bar_and(3, 128, mbar_wait_warp(&dq_full[s], (t >> 1) & 1, abort_flag, err, 10))) break;
       tc_fence_after();
       uint32_t a[32], c2[32];
       tmem_ld32(tmem + lane_base + L::kDQ + s * D, a);
@@ -386,18 +389,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&dq_free[s]);
-      const int i = qt * BQ + r;
-      if (i < p.seq_q) {
-        float* dst = p.dq_acc + ((int64_t)(b * p.heads + h) * p.seq_q + i) * D;
+      // stage the fp32 tile (two 32-column swizzled boxes), then one thread
+      // reduces it into the accumulator with the TMA engine
+      if (lane == 0 && warp == 12 && t > 0) bulk_wait_group_read0();
+      named_bar_sync(2, 128);
 #pragma unroll
-        for (int u = 0; u < 32; u += 4) {
-          red_add_v4(dst + u, __uint_as_float(a[u]), __uint_as_float(a[u + 1]), __uint_as_float(a[u + 2]),
-                     __uint_as_float(a[u + 3]));
-          red_add_v4(dst + 32 + u, __uint_as_float(c2[u]), __uint_as_float(c2[u + 1]), __uint_as_float(c2[u + 2]),
-                     __uint_as_float(c2[u + 3]));
+      for (int hb = 0; hb < 2; ++hb) {
+        const uint32_t* src = hb == 0 ? a : c2;
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const uint4 val = make_uint4(src[q4 * 4], src[q4 * 4 + 1], src[q4 * 4 + 2], src[q4 * 4 + 3]);
+          *reinterpret_cast<uint4*>(sDQ + hb * (128 * 128) + r * 128 + ((q4 ^ (r & 7)) << 4)) = val;
         }
       }
+      fence_proxy_async_smem();
+      named_bar_sync(2, 128);
+      if (lane == 0 && warp == 12) {
+        const int plane = b * p.heads + h;
+        tma_reduce_add_3d(&tm_dq, sDQ, 0, qt * BQ, plane);
+        tma_reduce_add_3d(&tm_dq, sDQ + 128 * 128, 32, qt * BQ, plane);
+        bulk_commit_group();
+      }
     }
+    if (lane == 0 && warp == 12) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
@@ -522,11 +536,12 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "cudaFuncSetAttribute(bwd tc)");
   const PolyPassArgs& f = a.fwd;
   BwdWs w = bwd_ws(a);
-  CUtensorMap tq, tdo, tk, tv;
+  CUtensorMap tq, tdo, tk, tv, tdq;
   int rc = make_map(&tq, f.q, f.dtype, D, f.seq_q, f.heads, f.batch, f.q_stride, BQ);
   if (!rc) rc = make_map(&tdo, a.dout, f.dtype, D, f.seq_q, f.heads, f.batch, a.dout_stride, BQ);
   if (!rc) rc = make_map(&tk, f.k, f.dtype, D, f.seq_k, f.kv_heads, f.batch, f.k_stride, BK);
   if (!rc) rc = make_map(&tv, f.v, f.dtype, D, f.seq_k, f.kv_heads, f.batch, f.v_stride, BK);
+  if (!rc) rc = make_map_f32_acc(&tdq, w.dq_acc, f.seq_q, f.batch * f.heads);
   if (rc) return rc;
   rc = cuda_status(cudaMemsetAsync(w.dq_acc, 0, (size_t)f.batch * f.heads * f.seq_q * D * 4, s), "memset dq acc");
   if (rc) return rc;
@@ -560,7 +575,7 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   p.dbias_stride[0] = a.dbias_stride[0];
   p.dbias_stride[1] = a.dbias_stride[1];
   dim3 grid((f.seq_k + BK - 1) / BK, f.batch * f.kv_heads);
-  pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, p);
+  pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
   const int64_t cthreads = (int64_t)f.batch * f.heads * f.seq_q * (D / 8);
   bwd_dq_convert_kernel<T><<<(unsigned)((cthreads + 255) / 256), 256, 0, s>>>(a, w.dq_acc);
   note_launch(3);
