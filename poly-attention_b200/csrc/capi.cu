@@ -65,10 +65,11 @@ unsigned long long poly_launch_count(void) { return g_launches.load(std::memory_
 
 int poly_device_error(int* out, int reset) {
   if (!out) return fail(POLY_EINVAL, "null out");
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   int rc = read_device_error_fwd(&a, reset != 0);
+  if (!rc) rc = read_device_error_fwd2(&c, reset != 0);
   if (!rc) rc = read_device_error_bwd(&b, reset != 0);
-  *out = a ? a : b;
+  *out = a ? a : (c ? c : b);
   return rc;
 }
 int poly_abi_version(void) { return POLY_ABI_VERSION; }

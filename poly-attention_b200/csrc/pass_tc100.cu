@@ -17,6 +17,7 @@
 //
 // Shared memory tiles are 128-byte swizzled (one 64-element atom per row
 // chunk); TMEM holds two S buffers (2 x 128 columns) and O (D columns).
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -463,6 +464,8 @@ bool pass_fwd_tc_eligible(const PolyPassArgs& a) {
 size_t pass_fwd_tc_workspace(const PolyPassArgs&) { return 0; }
 
 int launch_pass_fwd_tc(const PolyPassArgs& a, cudaStream_t s) {
+  const char* one = std::getenv("POLY_FWD_ONE_TILE");
+  if (!(one && one[0] == '1') && pass_fwd_tc2_eligible(a)) return launch_pass_fwd_tc2(a, s);
   if (a.dtype == POLY_BF16)
     return a.head_dim == 64 ? fwd_bias<64, __nv_bfloat16>(a, s) : fwd_bias<128, __nv_bfloat16>(a, s);
   return a.head_dim == 64 ? fwd_bias<64, __half>(a, s) : fwd_bias<128, __half>(a, s);
