@@ -40,6 +40,12 @@ def pass_fwd_flop(b):
     return 2 * 2 * (N * N / 2) * D * b * H
 
 
+# DRAM bytes per launch per batch element, from the ncu captures summarised in
+# profiles/ (batch-1 case; traffic scales with batch: every (b, h) reads its own
+# q/k/v once). pass_fwd_tc2: read 25.2 MB; pass_bwd_tc: read 50.9 MB.
+TRAFFIC_PER_BATCH = {"pass1_fwd": 25.23e6, "pass2_fwd": 25.49e6, "pass2_bwd": 50.9e6, "pass1_bwd": 50.9e6}
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -222,7 +228,9 @@ def run_ours(args, rank, world, local_rank):
         "frac_of_peak": step_flop / (ms_step * 1e-3) / 1e12 / sustained,
         "phases_ms": dict(zip(names, phases)),
         "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": sustained,
-                     "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": None,
+                     "unit": "TFLOP/s", "frac": achieved / sustained,
+                     "traffic": TRAFFIC_PER_BATCH[names[dom]] * b,
+                     "traffic_note": "ncu DRAM read+write bytes of a batch-1 capture x batch",
                      "peak_kind": f"{kind} bf16 sustained"},
         "e2e": e2e,
         "gpu_launches": int(launches),
