@@ -195,6 +195,7 @@ def run_ours(args, rank, world, local_rank):
         e2e = {"value": b * N * world / (float(te.item()) * 1e-3), "unit": "tokens/s",
                "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h in hosts),
                "d2h_bytes_per_step": sum(g.numel() * g.element_size() for g in grads_h)}
+    decode = None if args.no_decode else run_decode(args, dev)
     if world > 1:
         dist.barrier()
     if rank != 0:
@@ -236,7 +237,58 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
         "cpu_baseline": cpu_baseline() if (world == 1 and not args.no_cpu) else None,
+        "decode": decode,
     }
+
+
+def run_decode(args, dev):
+    """Config 4 decode: NPolyAttention order 3 core, batch 32, 16 query / 4 kv
+    heads, d 128, bf16; caches of 2048 positions (synthetic N(0,1) contents
+    stand in for the prefill), then 256 single-token steps through
+    ChainDecoder (in-place cache appends + one decode kernel pair per level)."""
+    import torch
+
+    from poly_attention_b200 import _lib
+    from poly_attention_b200.decode import ChainDecoder
+    b, h, g, d, order, L0, steps = 32, 16, 4, 128, 3, 2048, 256
+    dec = ChainDecoder(batch=b, order=order, heads=h, kv_heads=g, dim_head=d, capacity=L0 + steps + 8,
+                       dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(77)
+    for buf in dec.qs + dec.vs + dec.msgs:
+        buf[:, :, :L0].normal_(generator=gen)
+    for buf in dec.lses:
+        buf[:, :, :L0].normal_(generator=gen)
+    dec.length = L0
+    q1 = torch.randn(b, h, 1, d, device=dev, dtype=torch.bfloat16, generator=gen)
+    qn = [torch.randn(b, g, 1, d, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(order)]
+    vn = [torch.randn(b, g, 1, d, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(order - 1)]
+    out = torch.empty(b, h, 1, d, device=dev, dtype=torch.bfloat16)
+    for _ in range(3):  # warm-up steps, then rewind
+        dec.append_kv(qn, vn)
+        dec.step(q1, out)
+    dec.length = L0
+    torch.cuda.synchronize()
+    total_bytes = 0
+    n0 = _lib.launch_count()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        dec.append_kv(qn, vn)
+        dec.step(q1, out)
+        total_bytes += dec.bytes_per_step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e)
+    _, _, hbm, kind = peaks()
+    gbs = total_bytes / (ms * 1e-3) / 1e9
+    return {"metric": "decode tok/s", "value": b * steps / (ms * 1e-3), "unit": "tokens/s", "steps": steps,
+            "ms_per_step": ms / steps, "config": {"workload": "NPolyAttention order 3 core decode (config 4)",
+                                                  "batch": b, "heads": h, "kv_heads": g, "dim_head": d,
+                                                  "cache_len": f"{L0 + 1}..{L0 + steps}"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "traffic": None, "peak_kind": f"{kind} copy bandwidth",
+                         "bytes_note": "7 bf16 cache tensors + 2 fp32 lse caches at kv-head width per position"},
+            "gpu_launches": int(_lib.launch_count() - n0)}
 
 
 def cpu_unit_seconds():
@@ -287,6 +339,7 @@ def main():
     ap.add_argument("--batch", type=int, default=B, help="per-GPU batch (smaller for profiling captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))

@@ -83,3 +83,26 @@ def test_npoly_kv_cache_decode_matches_parallel(order, d):
     scale = float(np.abs(ref).max())
     np.testing.assert_allclose(host(par), ref, atol=ATOL * scale, rtol=RTOL)
     np.testing.assert_allclose(host(step), ref, atol=ATOL * scale, rtol=RTOL)
+
+
+@pytest.mark.parametrize("order,d,h,g", [(2, 64, 4, 2), (3, 128, 16, 4), (4, 64, 4, 4)])
+def test_chain_decoder_matches_parallel_oracle(order, d, h, g):
+    """Preallocated-cache decoding, one row per step, equals the oracle's
+    parallel causal chain (n_poly_attention.py:233-313)."""
+    from poly_attention_b200.decode import ChainDecoder
+    dt = torch.bfloat16
+    b, n = 2, 40
+    q1 = host(dev(rnd((b, h, n, d), 1), dt))
+    qs = [host(dev(rnd((b, g, n, d), 10 + t), dt)) for t in range(order)]
+    vs = [host(dev(rnd((b, g, n, d), 20 + t), dt)) for t in range(order - 1)]
+    dec = ChainDecoder(batch=b, order=order, heads=h, kv_heads=g, dim_head=d, capacity=64, dtype=dt)
+    outs = []
+    for i in range(n):
+        dec.append_kv([dev(x[:, :, i:i + 1], dt) for x in qs], [dev(x[:, :, i:i + 1], dt) for x in vs])
+        outs.append(host(dec.step(dev(q1[:, :, i:i + 1], dt))))
+    got = np.concatenate(outs, axis=2)
+    r = h // g
+    rep = lambda x: np.repeat(x, r, 1)  # noqa: E731
+    ref, _, _ = O.npoly_chain_fwd([q1] + [rep(x) for x in qs[:-1]], [rep(x) for x in qs], [rep(x) for x in vs],
+                                  causal=True)
+    np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
