@@ -291,6 +291,51 @@ def run_decode(args, dev):
             "gpu_launches": int(_lib.launch_count() - n0)}
 
 
+def run_longctx(args, rank, world, local_rank):
+    """Config 5: order-2 causal forward, b1 h16 n32768 d64 bf16, keys split
+    across the ranks (zig-zag shards, one max all-reduce + one reduce-scatter of
+    fp32 partials); total work fixed ("strong" scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from poly_attention_b200 import _lib
+    from poly_attention_b200.distributed import context_parallel_order2_fwd, zigzag_shard
+    b, h, n, d = 1, 16, 32768, 64
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    full = [torch.randn(b, h, n, d, device=dev, dtype=torch.bfloat16, generator=g) for _ in range(4)]
+    loc = [zigzag_shard(t, rank, world).contiguous() for t in full]
+    del full
+    for _ in range(args.warmup):
+        context_parallel_order2_fwd(*loc)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    n0 = _lib.launch_count()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        context_parallel_order2_fwd(*loc)
+    e.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if rank != 0:
+        return None
+    ms = float(t.item())
+    flop = 2 * 2 * 2 * (n * n / 2) * d * h * b            # two causal passes
+    sustained, _, _, kind = peaks()
+    return {"metric": "long-context order-2 fwd ms (config 5)", "value": ms, "unit": "ms", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "order-2 causal fwd, keys split across GPUs", "batch": b, "heads": h,
+                       "seq_len": n, "dim_head": d, "parallelism": f"cp{world} (zig-zag key split)"},
+            "tflops": flop / (ms * 1e-3) / 1e12, "frac_of_peak": flop / (ms * 1e-3) / 1e12 / (sustained * world),
+            "peak_kind": f"{kind} bf16 sustained x {world}", "gpu_launches_rank0": int(_lib.launch_count() - n0)}
+
+
 def cpu_unit_seconds():
     """Oracle (numpy, fp32) forward + backward of one (batch, head) unit of the workload."""
     import numpy as np
@@ -340,6 +385,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
+    ap.add_argument("--workload", choices=["train", "longctx"], default="train",
+                    help="train: config 2 fwd+bwd (the headline); longctx: config 5 key-split forward")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -353,7 +400,10 @@ def main():
             import torch.distributed as dist
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-        res = run_ours(args, rank, world, local_rank)
+        if args.workload == "longctx":
+            res = run_longctx(args, rank, world, local_rank)
+        else:
+            res = run_ours(args, rank, world, local_rank)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
