@@ -39,6 +39,7 @@ sys.path.insert(0, REF)
 
 from poly_attention.poly_attention import reference_poly_attention, Order2PolyAttention  # noqa: E402
 from poly_attention.n_poly_attention import NPolyAttention  # noqa: E402
+from poly_attention.poly_vit import PolyViT  # noqa: E402
 
 
 def np32(t):
@@ -221,8 +222,21 @@ def modn_cases():
         save(f"chain_grad_o{order}", **arrays)
 
 
+def vit_cases():
+    # PolyViT forward (poly_attention/poly_vit.py:65-101), order 2 and 3
+    for order in (2, 3):
+        torch.manual_seed(60 + order)
+        m = PolyViT(image_size=32, patch_size=8, num_classes=10, dim=64, depth=2, heads=4, mlp_dim=128,
+                    dim_head=16, order=order, use_flash_kernel=False if order == 2 else None)
+        img = torch.randn(2, 3, 32, 32)
+        with torch.no_grad():
+            y = m(img)
+        save(f"vit_o{order}", img=np32(img), y=np32(y), **{f"p:{k}": v for k, v in state_np(m).items()})
+
+
 if __name__ == "__main__":
     torch.set_num_threads(4)
     ref_fn_cases()
     mod2_cases()
     modn_cases()
+    vit_cases()

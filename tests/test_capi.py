@@ -93,3 +93,13 @@ def test_state_dict_names_match_reference(golden):
     ref_keys = {k[2:] for k in g if k.startswith("p:")}
     m = P.NPolyAttention(dim=64, order=3, heads=4, kv_heads=2, dim_head=16, causal=True)
     assert set(m.state_dict()) == ref_keys
+
+
+def test_polyvit_state_dict_names_match_reference(golden):
+    import poly_attention_b200 as P
+    for order in (2, 3):
+        g = golden(f"vit_o{order}")
+        ref_keys = {k[2:] for k in g if k.startswith("p:")}
+        m = P.PolyViT(image_size=32, patch_size=8, num_classes=10, dim=64, depth=2, heads=4, mlp_dim=128,
+                      dim_head=16, order=order)
+        assert set(m.state_dict()) == ref_keys

@@ -353,3 +353,16 @@ def test_tc_ragged_without_bias(nq, nk, causal):
     assert_close(dq, e[0], dtype, "dq")
     assert_close(dk, e[1], dtype, "dk")
     assert_close(dv, e[2], dtype, "dv")
+
+
+@pytest.mark.parametrize("order", [2, 3])
+def test_polyvit_golden(golden, order):
+    """PolyViT forward (poly_attention/poly_vit.py:65-101) vs the reference, fp32."""
+    import poly_attention_b200 as P
+    gd = golden(f"vit_o{order}")
+    m = P.PolyViT(image_size=32, patch_size=8, num_classes=10, dim=64, depth=2, heads=4, mlp_dim=128, dim_head=16,
+                  order=order)
+    m = load_module(m, gd)
+    with torch.no_grad():
+        y = m(dev(gd["img"]))
+    assert_close(y, gd["y"], torch.float32)
