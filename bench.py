@@ -336,6 +336,64 @@ def run_longctx(args, rank, world, local_rank):
             "peak_kind": f"{kind} bf16 sustained x {world}", "gpu_launches_rank0": int(_lib.launch_count() - n0)}
 
 
+def _time_module(fn, args, dev):
+    import torch
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / args.steps
+
+
+def run_module_configs(args, dev):
+    """Configs 1, 3 and the config-4 prefill through the drop-in modules
+    (projections / norms / MLPs in PyTorch, attention cores in libpolyattn)."""
+    import torch
+
+    import poly_attention_b200 as P
+    torch.manual_seed(0)
+    out = {}
+    if args.workload == "config1":
+        m = P.PolyAttention(dim=512, heads=8, dim_head=64, causal=False).to(dev)
+        x = torch.randn(1, 1024, 512, device=dev)
+        with torch.no_grad():
+            ms = _time_module(lambda: m(x), args, dev)
+        out = {"metric": "config 1 PolyAttention fp32 forward tokens/s", "value": 1024 / (ms * 1e-3),
+               "unit": "tokens/s", "ms_per_step": ms, "dtype": "f32",
+               "config": {"workload": "PolyAttention(dim=512, heads=8, dim_head=64) fwd, x [1, 1024, 512]"}}
+    elif args.workload == "vit":
+        m = P.PolyViT(image_size=256, patch_size=32, num_classes=1000, dim=1024, depth=6, heads=16, dim_head=64,
+                      mlp_dim=2048, order=2).to(dev, torch.bfloat16)
+        img = torch.randn(256, 3, 256, 256, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            ms = _time_module(lambda: m(img), args, dev)
+        flop = 2.01e12
+        sustained, _, _, kind = peaks()
+        out = {"metric": "config 3 PolyViT bf16 forward images/s", "value": 256 / (ms * 1e-3), "unit": "images/s",
+               "ms_per_step": ms, "dtype": "bf16", "tflops": flop / (ms * 1e-3) / 1e12,
+               "frac_of_peak": flop / (ms * 1e-3) / 1e12 / sustained,
+               "config": {"workload": "PolyViT(256/32, dim 1024, depth 6, heads 16, mlp 2048) fwd, batch 256",
+                          "tokens": "64 patches (the reference has no cls token)"}}
+    elif args.workload == "prefill4":
+        m = P.NPolyAttention(dim=2048, order=3, heads=16, kv_heads=4, dim_head=128, causal=True).to(
+            dev, torch.bfloat16)
+        x = torch.randn(32, 2048, 2048, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            ms = _time_module(lambda: m(x), args, dev)
+        out = {"metric": "config 4 NPolyAttention order-3 GQA prefill tokens/s", "value": 32 * 2048 / (ms * 1e-3),
+               "unit": "tokens/s", "ms_per_step": ms, "dtype": "bf16",
+               "config": {"workload": "NPolyAttention(dim=2048 assumed, order 3, h16, g4, d128, causal) fwd, "
+                                      "x [32, 2048, 2048]"}}
+    out.update({"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "data": "synthetic N(0,1), seeded",
+                "higher_is_better": True, "vs_baseline": None})
+    return out
+
+
 def cpu_unit_seconds():
     """Oracle (numpy, fp32) forward + backward of one (batch, head) unit of the workload."""
     import numpy as np
@@ -385,7 +443,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
-    ap.add_argument("--workload", choices=["train", "longctx"], default="train",
+    ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4"], default="train",
                     help="train: config 2 fwd+bwd (the headline); longctx: config 5 key-split forward")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -402,6 +460,9 @@ def main():
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
         if args.workload == "longctx":
             res = run_longctx(args, rank, world, local_rank)
+        elif args.workload in ("config1", "vit", "prefill4"):
+            import torch
+            res = run_module_configs(args, torch.device("cuda", local_rank)) if rank == 0 else None
         else:
             res = run_ours(args, rank, world, local_rank)
         if world > 1:
