@@ -105,6 +105,51 @@ __device__ __forceinline__ void store_chunk(uint8_t* tile, int r, int c, const u
   }
 }
 
+// One 32-query chunk of the softmax backward for this thread's key row.
+// x = s * scale * log2(e) + bias - lse (log2 domain), p = 2^x,
+// ds = p (dp - delta), d-bias += ds, dS = ds * softclamp'(s). MASK adds the
+// causal diagonal (queries il < diag_row) and invalid-key masks; the
+// unmasked variant is the common case and carries no per-element selects.
+template <typename T, bool SOFTCLAMP, bool HAS_BIAS, bool MASK>
+__device__ __forceinline__ void softmax_bwd_chunk(const uint32_t (&sv)[32], const uint32_t (&dv)[32],
+                                                  const float* nl, const float* dl, float b2, const BwdParams& p,
+                                                  bool key_ok, int il0, int diag_row, float& dbias,
+                                                  uint32_t (&pw)[16], uint32_t (&dw)[16]) {
+  const float4* l4 = reinterpret_cast<const float4*>(nl);
+  const float4* d4 = reinterpret_cast<const float4*>(dl);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 lq = l4[q], dq = d4[q];
+    const float lv[4] = {lq.x, lq.y, lq.z, lq.w};
+    const float dd4[4] = {dq.x, dq.y, dq.z, dq.w};
+    float pp[4], dd[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int u = q * 4 + e;
+      const float sr = __uint_as_float(sv[u]);
+      const float off = HAS_BIAS ? lv[e] + b2 : lv[e];
+      float x, dfac = 1.f;
+      if (SOFTCLAMP) {
+        const float th = tanhf(sr * p.sc_in);
+        dfac = 1.f - th * th;
+        x = fmaf(th, p.sc_out, off);
+      } else {
+        x = fmaf(sr, p.sl2, off);
+      }
+      float pr = ex2(x);
+      if (MASK && (!key_ok || il0 + u < diag_row)) pr = 0.f;
+      const float ds = pr * (__uint_as_float(dv[u]) - dd4[e]);
+      dbias += ds;
+      pp[e] = pr;
+      dd[e] = SOFTCLAMP ? ds * dfac : ds;
+    }
+    pw[2 * q] = pk<T>(pp[0], pp[1]);
+    pw[2 * q + 1] = pk<T>(pp[2], pp[3]);
+    dw[2 * q] = pk<T>(dd[0], dd[1]);
+    dw[2 * q + 1] = pk<T>(dd[2], dd[3]);
+  }
+}
+
 template <typename T, bool SOFTCLAMP, bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1)
     pass_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -268,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int j = kt * BK + r;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const bool key_ok = j < p.seq_k;
+    const bool key_ok_warp = __all_sync(0xffffffffu, key_ok);
     float b2 = 0.f;
     if (HAS_BIAS && key_ok) {
       const float braw = p.bias[b * p.bias_stride[0] + kvh * p.bias_stride[1] + j];
@@ -289,40 +335,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + lane_base + L::kS + c * 32, sv);
         tmem_ld32(tmem + lane_base + L::kDP + c * 32, dv);
         tmem_wait_ld();
-        const float4* l4 = reinterpret_cast<const float4*>(sLse + s * BQ + c * 32);
-        const float4* d4 = reinterpret_cast<const float4*>(sDel + s * BQ + c * 32);
         uint32_t pw[16], dw[16];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 lq = l4[q], dq = d4[q];
-          const float lv[4] = {lq.x, lq.y, lq.z, lq.w};
-          const float dl[4] = {dq.x, dq.y, dq.z, dq.w};
-          float pp[4], dd[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int u = q * 4 + e;
-            const int il = c * 32 + u;
-            const float sr = __uint_as_float(sv[u]);
-            float x, dfac = 1.f;
-            if (SOFTCLAMP) {
-              const float th = tanhf(sr * p.sc_in);
-              dfac = 1.f - th * th;
-              x = th * p.sc_out;
-            } else {
-              x = sr * p.sl2;
-            }
-            float pr = ex2(x + (b2 - lv[e]));
-            if (!key_ok || (diag && il < r)) pr = 0.f;
-            const float ds = pr * (__uint_as_float(dv[u]) - dl[e]);
-            dbias += ds;
-            pp[e] = pr;
-            dd[e] = SOFTCLAMP ? ds * dfac : ds;
-          }
-          pw[2 * q] = pk<T>(pp[0], pp[1]);
-          pw[2 * q + 1] = pk<T>(pp[2], pp[3]);
-          dw[2 * q] = pk<T>(dd[0], dd[1]);
-          dw[2 * q + 1] = pk<T>(dd[2], dd[3]);
-        }
+        const float* nl = sLse + s * BQ + c * 32;       // -lse2 of the chunk's queries
+        const float* dl = sDel + s * BQ + c * 32;
+        if (diag || !key_ok_warp)
+          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, true>(sv, dv, nl, dl, b2, p, key_ok, c * 32, diag ? r : -1,
+                                                          dbias, pw, dw);
+        else
+          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, false>(sv, dv, nl, dl, b2, p, key_ok, c * 32, -1, dbias, pw,
+                                                           dw);
         // P^T / dS^T smem is free once the previous tile's MMAs completed
         if (cc == 0 && t > 0 && !mbar_wait_warp(mma_done, (t - 1) & 1, abort_flag, err, 8)) {
           ok = false;
@@ -425,8 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// delta_i = dout_i . out_i - dlse_i and lse2_i = lse_i * log2(e), padded to
-// nq_pad rows per (batch, head) with (delta 0, lse2 +inf) so padded queries
+// delta_i = dout_i . out_i - dlse_i and nlse2_i = -lse_i * log2(e), padded to
+// nq_pad rows per (batch, head) with (delta 0, nlse2 -inf) so padded queries
 // get p = 0. Eight lanes per row, 16-byte loads.
 template <typename T>
 __global__ void bwd_prep_kernel(const PolyPassBwdArgs a, float* lse2, float* delta, int nq_pad) {
@@ -455,12 +476,12 @@ __global__ void bwd_prep_kernel(const PolyPassBwdArgs a, float* lse2, float* del
   s += __shfl_xor_sync(0xffffffffu, s, 4);
   if (sub == 0) {
     if (i >= a.fwd.seq_q) {
-      lse2[w] = INFINITY;
+      lse2[w] = -INFINITY;      // stored negated: padded queries get p = 2^-inf = 0
       delta[w] = 0.f;
     } else {
       if (a.dlse) s -= a.dlse[b * a.dlse_stride[0] + h * a.dlse_stride[1] + i];
       delta[w] = s;
-      lse2[w] = a.fwd.lse[b * a.fwd.lse_stride[0] + h * a.fwd.lse_stride[1] + i] * kLog2e;
+      lse2[w] = -a.fwd.lse[b * a.fwd.lse_stride[0] + h * a.fwd.lse_stride[1] + i] * kLog2e;
     }
   }
 }
