@@ -266,6 +266,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool tail = (j == kt_total - 1) && (p.seq_k % BN) != 0;
       const bool diag = p.causal && (j == diag_tile);
       float tmax = -INFINITY;
+      // Without a bias the row max is taken on the raw scores and the scale is
+      // folded into the exponent's FFMA; with a bias x = s * scale * log2e + b
+      // is formed first. Both end with v[] holding values whose 2^(v*mul - m)
+      // is the unnormalised probability.
+      float mul = 1.f;
       if (HAS_BIAS) {
         const float4* b4 = reinterpret_cast<const float4*>(sB + s * BN);
 #pragma unroll
@@ -277,8 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           v[4 * q + 3] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 3]), p.sl2, bb.w * kLog2e));
         }
       } else {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * p.sl2);
+        mul = p.sl2;
       }
       if (tail) {
         const int kvalid = p.seq_k - j * BN;
@@ -291,16 +295,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BN; ++c)
           if (c > r) v[c] = __float_as_uint(-INFINITY);
       }
+      {
+        float mx[4];
 #pragma unroll
-      for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, __uint_as_float(v[c]));
+        for (int u = 0; u < 4; ++u) mx[u] = __uint_as_float(v[u]);
+#pragma unroll
+        for (int c = 4; c < BN; ++c) mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(v[c]));
+        tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * mul;
+      }
       const float m_new = fmaxf(m_run, tmax);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = ex2(m_run - m_use);
       float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        const float e0 = ex2(__uint_as_float(v[c]) - m_use);
-        const float e1 = ex2(__uint_as_float(v[c + 1]) - m_use);
+        const float e0 = ex2(fmaf(__uint_as_float(v[c]), mul, -m_use));
+        const float e1 = ex2(fmaf(__uint_as_float(v[c + 1]), mul, -m_use));
         sum0 += e0;
         sum1 += e1;
         v[c >> 1] = pk2<T>(e0, e1);              // packed P overwrites the consumed half
