@@ -303,7 +303,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 4; c < BN; ++c) mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(v[c]));
         tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * mul;
       }
-      const float m_new = fmaxf(m_run, tmax);
+      // Lazy rescaling: the reference max only moves when the row max grows
+      // by more than 2^8 (log2 domain), so P <= 256 and O is rarely rescaled;
+      // lse = m_run + log2(l) stays exact.
+      const bool grow = tmax > m_run + 8.f;
+      const float m_new = grow ? tmax : m_run;
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = ex2(m_run - m_use);
       float sum0 = 0.f, sum1 = 0.f;
@@ -320,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j > 0) {
         if (!mbar_wait_warp(&o_done[x], (j - 1) & 1, abort_flag, err, 50)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
