@@ -250,7 +250,8 @@ def run_decode(args, dev):
 
     from poly_attention_b200 import _lib
     from poly_attention_b200.decode import ChainDecoder
-    b, h, g, d, order, L0, steps = 32, 16, 4, 128, 3, 2048, 256
+    b, h, g, d, order, L0 = 32, 16, 4, 128, 3, 2048
+    steps = 256 if args.workload != "decode" else max(1, args.steps)
     dec = ChainDecoder(batch=b, order=order, heads=h, kv_heads=g, dim_head=d, capacity=L0 + steps + 8,
                        dtype=torch.bfloat16, device=dev)
     gen = torch.Generator(device=dev).manual_seed(77)
@@ -443,7 +444,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
-    ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4"], default="train",
+    ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4", "decode"], default="train",
                     help="train: config 2 fwd+bwd (the headline); longctx: config 5 key-split forward")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -460,6 +461,9 @@ def main():
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
         if args.workload == "longctx":
             res = run_longctx(args, rank, world, local_rank)
+        elif args.workload == "decode":
+            import torch
+            res = run_decode(args, torch.device("cuda", local_rank)) if rank == 0 else None
         elif args.workload in ("config1", "vit", "prefill4"):
             import torch
             res = run_module_configs(args, torch.device("cuda", local_rank)) if rank == 0 else None
