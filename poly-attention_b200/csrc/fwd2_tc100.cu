@@ -9,7 +9,9 @@
 //
 // Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 4-7 softmax A,
 // 8-11 softmax B. TMEM columns: S_A [0,128), S_B [128,256), O_A [256,320),
-// O_B [320,384).
+// O_B [320,384), P_A [384,448), P_B [448,512). P (16-bit, two per column)
+// stays in TMEM and is the A operand of the P V MMA, so no probability tile
+// crosses shared memory (shared-memory operand bandwidth bounds SS MMAs).
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -45,8 +47,7 @@ struct L2 {
   static constexpr int kQ = 0;                // 2 tiles
   static constexpr int kK = kQ + 2 * kTile;   // S stages
   static constexpr int kV = kK + S * kTile;
-  static constexpr int kP = kV + S * kTile;   // 2 x [128][128] 16-bit = 2 x 32 KB
-  static constexpr int kB = kP + 4 * kTile;   // S x 128 fp32 bias
+  static constexpr int kB = kV + S * kTile;   // S x 128 fp32 bias
   static constexpr int kBar = kB + S * BN * 4;
   static constexpr int kNumBars = 1 + 3 * S + 2 * 4 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
@@ -105,7 +106,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem + L2::kQ;
   uint8_t* sK = smem + L2::kK;
   uint8_t* sV = smem + L2::kV;
-  uint8_t* sP = smem + L2::kP;
   float* sB = (float*)(smem + L2::kB);
   uint64_t* bars = (uint64_t*)(smem + L2::kBar);
   uint64_t* q_full = bars;
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------------------------ MMA issuer
       constexpr uint32_t idS = idesc_f16(BM, BN, kIsBf16, 0, 0);
       constexpr uint32_t idO = idesc_f16(BM, D, kIsBf16, 0, 1);
-      const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sP);
+      const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK), va = smem_u32(sV);
       auto issue_s = [&](int x, int j) {
         const int s = j % S;
 #pragma unroll
@@ -197,11 +197,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_pv = [&](int x, int j) {
         const int s = j % S;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t aoff = (uint32_t)(kk >> 2) * (BM * 128) + (uint32_t)(kk & 3) * 32;
-          mma_f16_ss(tmem + 256 + x * D, smem_desc_sw128(pa + x * 2 * L2::kTile + aoff, 16, 1024),
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_f16_ts(tmem + 256 + x * D, tmem + 384 + x * 64 + kk * 8,
                      smem_desc_sw128(va + s * L2::kTile + kk * 2048, BN * 128, 1024), idO, (j > 0 || kk > 0));
-        }
         mma_commit(&o_done[x]);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, err, 42) && mbar_wait(&k_full[0], 0, abort_flag, err, 43);
@@ -249,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int diag_tile = 2 * mt + x;             // causal: the key tile on this tile's diagonal
     const uint32_t s_addr = tmem + lane_base + x * BN;
     const uint32_t o_addr = tmem + lane_base + 256 + x * D;
-    uint8_t* myP = sP + x * 2 * L2::kTile;
+    const uint32_t p_addr = tmem + lane_base + 384 + x * 64;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
@@ -337,13 +335,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
         }
       }
-#pragma unroll
-      for (int c = 0; c < BN / 8; ++c) {
-        const int atom = c >> 3, cc = c & 7;
-        *reinterpret_cast<uint4*>(myP + atom * (BM * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) =
-            make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-      }
-      fence_proxy_async_smem();
+      // packed P (64 columns of bf16x2) -> TMEM, the A operand of P V
+      tmem_st32(p_addr, *reinterpret_cast<const uint32_t(*)[32]>(&v[0]));
+      tmem_st32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&v[32]));
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[x]);
     }
