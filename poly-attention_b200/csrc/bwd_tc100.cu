@@ -53,8 +53,7 @@ struct BwdLayout {
   static constexpr int kV = kK + kTile;
   static constexpr int kQ = kV + kTile;          // 2 stages
   static constexpr int kDO = kQ + 2 * kTile;     // 2 stages
-  static constexpr int kPT = kDO + 2 * kTile;    // [128 keys][128 queries]
-  static constexpr int kDST = kPT + 2 * kTile;
+  static constexpr int kDST = kDO + 2 * kTile;   // dS^T [128 keys][128 queries], read MN-major by dQ
   static constexpr int kDQS = kDST + 2 * kTile;  // dQ staging: 2 x [128 rows][32 fp32], swizzled
   static constexpr int kLse = kDQS + 2 * kTile;  // 2 stages x 128 floats
   static constexpr int kDel = kLse + 2 * BQ * 4;
@@ -65,7 +64,8 @@ struct BwdLayout {
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 320, kDQ = 384;  // kDQ: 2 x 64
+  // P^T (16-bit, two queries per column) lives in TMEM as the A operand of dV += P^T dO
+  static constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 320, kDQ = 384, kPT = 448;
 };
 
 struct BwdParams {
@@ -163,7 +163,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + L::kV;
   uint8_t* sQ = smem + L::kQ;
   uint8_t* sDO = smem + L::kDO;
-  uint8_t* sPT = smem + L::kPT;
   uint8_t* sDST = smem + L::kDST;
   uint8_t* sDQ = smem + L::kDQS;
   float* sLse = (float*)(smem + L::kLse);
@@ -255,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idKV = idesc_f16(128, D, kIsBf16, 0, 1);     // P^T / dS^T  x  dO / Q (MN)
       constexpr uint32_t idQ = idesc_f16(128, D, kIsBf16, 1, 1);      // dS (MN view) x K (MN)
       const uint32_t ka = smem_u32(sK), va = smem_u32(sV), qa = smem_u32(sQ), doa = smem_u32(sDO);
-      const uint32_t pta = smem_u32(sPT), dsa = smem_u32(sDST);
+      const uint32_t dsa = smem_u32(sDST);
       auto issue_sdp = [&](int s) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -284,21 +283,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < BQ / 16; ++kk) {
           const uint32_t aoff = (uint32_t)(kk >> 2) * (128 * 128) + (uint32_t)(kk & 3) * 32;
           const uint32_t acc = (t > 0 || kk > 0);
-          mma_f16_ss(tmem + L::kDV, smem_desc_sw128(pta + aoff, 16, 1024),
+          mma_f16_ts(tmem + L::kDV, tmem + L::kPT + kk * 8,
                      smem_desc_sw128(doa + s * L::kTile + kk * 2048, 128 * 128, 1024), idKV, acc);
           mma_f16_ss(tmem + L::kDK, smem_desc_sw128(dsa + aoff, 16, 1024),
                      smem_desc_sw128(qa + s * L::kTile + kk * 2048, 128 * 128, 1024), idKV, acc);
         }
-        if (t >= 2 && !mbar_wait(&dq_free[s], ((t >> 1) - 1) & 1, abort_flag, err, 6)) break;
+        if (t >= 1 && !mbar_wait(&dq_free[0], (t - 1) & 1, abort_flag, err, 6)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          mma_f16_ss(tmem + L::kDQ + s * D, smem_desc_sw128(dsa + kk * 2048, 128 * 128, 1024),
+          mma_f16_ss(tmem + L::kDQ, smem_desc_sw128(dsa + kk * 2048, 128 * 128, 1024),
                      smem_desc_sw128(ka + kk * 2048, 128 * 128, 1024), idQ, kk > 0);
         }
         mma_commit(&q_empty[s]);
         mma_commit(mma_done);
-        mma_commit(&dq_full[s]);
+        mma_commit(&dq_full[0]);
       }
       mma_commit(dkv_done);
       mma_commit(drain);
@@ -349,10 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        store_chunk(sPT, r, c, pw);
+        tmem_st16(tmem + lane_base + L::kPT + c * 16, pw);   // queries c*32.. -> 16 packed columns
         store_chunk(sDST, r, c, dw);
       }
       if (!ok) break;
+      tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_ready);
@@ -398,18 +398,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     for (int t = 0; t < NT; ++t) {
-      const int s = t & 1;
       int h, qt;
       tile_of(t, h, qt);
       // exit decision shared by the whole warpgroup (it meets at named barriers)
-      if (!named_bar_and(3, 128, mbar_wait_warp(&dq_full[s], (t >> 1) & 1, abort_flag, err, 10))) break;
+      if (!named_bar_and(3, 128, mbar_wait_warp(&dq_full[0], t & 1, abort_flag, err, 10))) break;
       tc_fence_after();
       uint32_t a[32], c2[32];
-      tmem_ld32(tmem + lane_base + L::kDQ + s * D, a);
-      tmem_ld32(tmem + lane_base + L::kDQ + s * D + 32, c2);
+      tmem_ld32(tmem + lane_base + L::kDQ, a);
+      tmem_ld32(tmem + lane_base + L::kDQ + 32, c2);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&dq_free[s]);
+      mbar_arrive(&dq_free[0]);
       // stage the fp32 tile (two 32-column swizzled boxes), then one thread
       // reduces it into the accumulator with the TMA engine
       if (lane == 0 && warp == 12 && t > 0) bulk_wait_group_read0();
