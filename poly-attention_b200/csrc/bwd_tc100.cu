@@ -45,7 +45,7 @@ using namespace tc;
 constexpr int D = 64;
 constexpr int BK = 128;   // keys per CTA
 constexpr int BQ = 128;   // queries per tile
-constexpr int kThreads = 512;
+constexpr int kThreads = 384;
 
 struct BwdLayout {
   static constexpr int kTile = 128 * D * 2;  // 16 KB: one [128][64] 16-bit tile
@@ -220,6 +220,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     h = kvh * rep + hr;
   };
 
+  // dQ of tile t: TMEM -> swizzled fp32 smem tile -> one TMA reduce-add into
+  // the accumulator. Run by softmax warpgroup 0 (warps 4-7, all four TMEM lane
+  // quarters) right after it has handed tile t + 1 to the MMA. Returns false
+  // if a wait gave up; the decision is shared by the warpgroup.
+  auto stage_dq = [&](int t) -> bool {
+    int h, qt;
+    tile_of(t, h, qt);
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    if (!named_bar_and(3, 128, mbar_wait_warp(&dq_full[0], t & 1, abort_flag, err, 10))) return false;
+    tc_fence_after();
+    uint32_t a[32], c2[32];
+    tmem_ld32(tmem + lane_base + L::kDQ, a);
+    tmem_ld32(tmem + lane_base + L::kDQ + 32, c2);
+    tmem_wait_ld();
+    tc_fence_before();
+    mbar_arrive(&dq_free[0]);
+    if (lane == 0 && warp == 4 && t > 0) bulk_wait_group_read0();
+    named_bar_sync(2, 128);
+#pragma unroll
+    for (int hb = 0; hb < 2; ++hb) {
+      const uint32_t* src = hb == 0 ? a : c2;
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4) {
+        const uint4 val = make_uint4(src[q4 * 4], src[q4 * 4 + 1], src[q4 * 4 + 2], src[q4 * 4 + 3]);
+        *reinterpret_cast<uint4*>(sDQ + hb * (128 * 128) + r * 128 + ((q4 ^ (r & 7)) << 4)) = val;
+      }
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(2, 128);
+    if (lane == 0 && warp == 4) {
+      const int plane = b * p.heads + h;
+      tma_reduce_add_3d(&tm_dq, sDQ, 0, qt * BQ, plane);
+      tma_reduce_add_3d(&tm_dq, sDQ + 128 * 128, 32, qt * BQ, plane);
+      bulk_commit_group();
+    }
+    return true;
+  };
+
   if (warp == 0) {
     if (lane == 0 && NT > 0) {
       // ------------------------------------------------ TMA producer
@@ -356,7 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_ready);
+      if (hw == 0 && t > 0 && !stage_dq(t - 1)) { ok = false; break; }
     }
+    if (hw == 0 && ok && NT > 0 && !stage_dq(NT - 1)) ok = false;
+    if (hw == 0 && lane == 0 && warp == 4) bulk_wait_group0();
     // dK (warpgroup 0) or dV (warpgroup 1) for this key row. tcgen05.ld is
     // warp-collective: every lane runs it; only the stores depend on key_ok.
     bool have = ok && NT > 0 && mbar_wait_warp(dkv_done, 0, abort_flag, err, 9);
@@ -393,45 +435,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (hw == 1) sDb[r] = dbias;
     dbias_part = dbias;
-  } else if (warp >= 12) {
-    // -------------------------------------------------- dQ reduction (thread = query row)
-    const int r = (warp & 3) * 32 + lane;
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    for (int t = 0; t < NT; ++t) {
-      int h, qt;
-      tile_of(t, h, qt);
-      // exit decision shared by the whole warpgroup (it meets at named barriers)
-      if (!named_bar_and(3, 128, mbar_wait_warp(&dq_full[0], t & 1, abort_flag, err, 10))) break;
-      tc_fence_after();
-      uint32_t a[32], c2[32];
-      tmem_ld32(tmem + lane_base + L::kDQ, a);
-      tmem_ld32(tmem + lane_base + L::kDQ + 32, c2);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&dq_free[0]);
-      // stage the fp32 tile (two 32-column swizzled boxes), then one thread
-      // reduces it into the accumulator with the TMA engine
-      if (lane == 0 && warp == 12 && t > 0) bulk_wait_group_read0();
-      named_bar_sync(2, 128);
-#pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        const uint32_t* src = hb == 0 ? a : c2;
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) {
-          const uint4 val = make_uint4(src[q4 * 4], src[q4 * 4 + 1], src[q4 * 4 + 2], src[q4 * 4 + 3]);
-          *reinterpret_cast<uint4*>(sDQ + hb * (128 * 128) + r * 128 + ((q4 ^ (r & 7)) << 4)) = val;
-        }
-      }
-      fence_proxy_async_smem();
-      named_bar_sync(2, 128);
-      if (lane == 0 && warp == 12) {
-        const int plane = b * p.heads + h;
-        tma_reduce_add_3d(&tm_dq, sDQ, 0, qt * BQ, plane);
-        tma_reduce_add_3d(&tm_dq, sDQ + 128 * 128, 32, qt * BQ, plane);
-        bulk_commit_group();
-      }
-    }
-    if (lane == 0 && warp == 12) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
