@@ -185,6 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* err = &g_poly_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // grid: x = key tile (fast), y = (batch, kv head): the CTAs of one head run
+  // together and share its Q / dO stream in L2 (heads-fast order was slower)
   const int kt = blockIdx.x;
   const int b = blockIdx.y / p.kv_heads, kvh = blockIdx.y - b * p.kv_heads;
   const int rep = p.heads / p.kv_heads;

@@ -122,9 +122,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* err = &g_poly_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y / p.heads, h = blockIdx.y - b * p.heads;
+  // grid: x = (batch, head), y = query-tile pair, heaviest (most key tiles)
+  // first, so the dispatch order is longest-first across all heads
+  const int b = blockIdx.x / p.heads, h = blockIdx.x - b * p.heads;
   const int kvh = h / (p.heads / p.kv_heads);
-  const int mt = p.causal ? (p.m_tiles - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+  const int mt = p.causal ? (p.m_tiles - 1 - (int)blockIdx.y) : (int)blockIdx.y;
   const int row0 = mt * 2 * BM;
   const int kt_total = (p.seq_k + BN - 1) / BN;
   // key tiles seen by tile A (rows row0..) and tile B (rows row0 + 128..)
@@ -440,7 +442,7 @@ int launch_t(const PolyPassArgs& a, cudaStream_t st) {
   }
   p.lse_stride[0] = a.lse_stride[0];
   p.lse_stride[1] = a.lse_stride[1];
-  dim3 grid(p.m_tiles, a.batch * a.heads);
+  dim3 grid(a.batch * a.heads, p.m_tiles);
   pass_fwd_tc2_kernel<T, HAS_BIAS><<<grid, kThreads, L2::kAlloc, st>>>(tq, tk, tv, tb, p);
   note_launch(1);
   return cuda_status(cudaGetLastError(), "pass_fwd_tc2 launch");

@@ -139,9 +139,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   int* err = &g_poly_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y / p.heads, h = blockIdx.y - b * p.heads;
+  // grid: x = (batch, head), y = query tile, heaviest first (longest-first dispatch)
+  const int b = blockIdx.x / p.heads, h = blockIdx.x - b * p.heads;
   const int kvh = h / (p.heads / p.kv_heads);
-  const int mt = p.causal ? (p.m_tiles - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+  const int mt = p.causal ? (p.m_tiles - 1 - (int)blockIdx.y) : (int)blockIdx.y;
   const int row0 = mt * BM;
   const int kt_total = (p.seq_k + BN - 1) / BN;
   const int nt = p.causal ? min(kt_total, mt + 1) : kt_total;
@@ -432,7 +433,7 @@ int launch_fwd_tc_t(const PolyPassArgs& a, cudaStream_t s) {
   p.lse_stride[1] = a.lse_stride[1];
   p.epi_mul = a.epi_mul;
   p.epi_out = a.epi_out;
-  dim3 grid(p.m_tiles, a.batch * a.heads);
+  dim3 grid(a.batch * a.heads, p.m_tiles);
   pass_fwd_tc_kernel<D, T, HAS_BIAS, SOFTCLAMP><<<grid, kFwdThreads, L::kAlloc, s>>>(tq, tk, tv, p);
   note_launch(1);
   return cuda_status(cudaGetLastError(), "pass_fwd_tc launch");
