@@ -46,6 +46,7 @@ constexpr int D = 64;
 constexpr int BK = 128;   // keys per CTA
 constexpr int BQ = 128;   // queries per tile
 constexpr int kThreads = 384;
+constexpr int kHeadGroup = 8;
 
 struct BwdLayout {
   static constexpr int kTile = 128 * D * 2;  // 16 KB: one [128][64] 16-bit tile
@@ -69,7 +70,7 @@ struct BwdLayout {
 };
 
 struct BwdParams {
-  int seq_q, seq_k, heads, kv_heads, nq_pad, q_tiles, causal;
+  int seq_q, seq_k, heads, kv_heads, nq_pad, q_tiles, k_tiles, causal;
   float scale, sl2, sc_in, sc_out;
   const float* bias; int64_t bias_stride[2];
   float* dq_acc;                 // [b*heads][seq_q][64] fp32
@@ -185,10 +186,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* err = &g_poly_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // grid: x = key tile (fast), y = (batch, kv head): the CTAs of one head run
-  // together and share its Q / dO stream in L2 (heads-fast order was slower)
-  const int kt = blockIdx.x;
-  const int b = blockIdx.y / p.kv_heads, kvh = blockIdx.y - b * p.kv_heads;
+  // 1-D grid over (head group of kHeadGroup (batch, kv head)s, key tile,
+  // head in group): heaviest key tiles first within a group (longest-first
+  // dispatch), while the CTAs running together cover only a few heads, whose
+  // Q / dO streams stay in L2.
+  int kt, bh;
+  {
+    const int nkt = p.k_tiles, nbh = gridDim.x / p.k_tiles;
+    const int lin = blockIdx.x;
+    const int grp = lin / (kHeadGroup * nkt);
+    const int gsz = min(kHeadGroup, nbh - grp * kHeadGroup);
+    const int rem = lin - grp * kHeadGroup * nkt;
+    kt = rem / gsz;
+    bh = grp * kHeadGroup + (rem - kt * gsz);
+  }
+  const int b = bh / p.kv_heads, kvh = bh - b * p.kv_heads;
   const int rep = p.heads / p.kv_heads;
   const int qt0 = p.causal ? kt : 0;
   const int nqt = max(0, p.q_tiles - qt0);
@@ -599,7 +611,8 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   p.dbias = a.dbias;
   p.dbias_stride[0] = a.dbias_stride[0];
   p.dbias_stride[1] = a.dbias_stride[1];
-  dim3 grid((f.seq_k + BK - 1) / BK, f.batch * f.kv_heads);
+  p.k_tiles = (f.seq_k + BK - 1) / BK;
+  dim3 grid(p.k_tiles * f.batch * f.kv_heads);
   pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
   const int64_t cthreads = (int64_t)f.batch * f.heads * f.seq_q * (D / 8);
   bwd_dq_convert_kernel<T><<<(unsigned)((cthreads + 255) / 256), 256, 0, s>>>(a, w.dq_acc);
