@@ -366,3 +366,25 @@ def test_polyvit_golden(golden, order):
     with torch.no_grad():
         y = m(dev(gd["img"]))
     assert_close(y, gd["y"], torch.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("d", [32, 128])
+def test_pass_bwd_other_head_dims(dtype, d):
+    """Backward at head sizes the tensor-core backward does not take (CUDA-core path)."""
+    import poly_attention_b200 as P
+    b, h, g, n = 1, 4, 2, 70
+    q = quant(rnd((b, h, n, d), 1), dtype)
+    k, v = (quant(rnd((b, g, n, d), s), dtype) for s in (2, 3))
+    do = quant(rnd((b, h, n, d), 4), dtype)
+    qt, kt, vt = dev(q, dtype), dev(k, dtype), dev(v, dtype)
+    assert P.kernel_names(qt, kt, vt, causal=True)[1] == "simt"
+    out, lse = P.pass_fwd(qt, kt, vt, causal=True)
+    dq, dk, dv, _ = P.pass_bwd(qt, kt, vt, out, lse, dev(do, dtype), causal=True)
+    r = h // g
+    e = O._pass_bwd(q, np.repeat(k, r, 1), np.repeat(v, r, 1), do, scale=d ** -0.5, causal=True,
+                    softclamp_value=None, key_mask=None, query_mask=None, bias=None)
+    group = lambda t: t.reshape(b, g, r, *t.shape[2:]).sum(2)  # noqa: E731
+    assert_close(dq, e[0], dtype, "dq")
+    assert_close(dk, group(e[1]), dtype, "dk")
+    assert_close(dv, group(e[2]), dtype, "dv")
