@@ -23,6 +23,9 @@
  *                     at :409-422 and :429-442) plus the dq2 sum at :444
  *   poly_lse_merge <- no counterpart: merges key-split partial passes (the
  *                     long-context sequence split across GPUs)
+ *   poly_decode_chain <- the cached passes of one decoding step, run level
+ *                     after level (poly_attention/n_poly_attention.py:263-313,
+ *                     poly_attention/poly_attention.py:63-114 with cache)
  */
 #ifndef POLY_ATTENTION_H_
 #define POLY_ATTENTION_H_
@@ -154,6 +157,20 @@ POLY_API int poly_pass_bwd(const PolyPassBwdArgs* args, void* stream);
 POLY_API size_t poly_pass_bwd_workspace_size(const PolyPassBwdArgs* args);
 
 POLY_API int poly_lse_merge(const PolyMergeArgs* args, void* stream);
+
+/*
+ * The n passes of one KV-cache decoding step of the order-n chain, in order,
+ * in one call. Contract: passes[i + 1] reads what passes[i] wrote only in the
+ * LAST key row (row seq_k - 1, the row the step appended) of its v, v_mul and
+ * bias; every other input is complete when the call is made (stream order);
+ * no pass writes what an earlier pass of the list reads. Under it, each pass
+ * after the first is launched as a programmatic dependent of the previous one:
+ * its CTAs start while the previous pass drains, stream every key tile but the
+ * last, and wait for the previous pass before loading the last. Every pass
+ * must take the decode kernel (poly_pass_fwd_kernel_name() == "decode"), else
+ * POLY_EUNSUPPORTED and nothing is launched. No workspace is used.
+ */
+POLY_API int poly_decode_chain(const PolyPassArgs* passes, int n, void* stream);
 
 /*
  * poly_pass_bwd without a caller workspace. No counterpart in the reference:

@@ -65,11 +65,12 @@ unsigned long long poly_launch_count(void) { return g_launches.load(std::memory_
 
 int poly_device_error(int* out, int reset) {
   if (!out) return fail(POLY_EINVAL, "null out");
-  int a = 0, b = 0, c = 0;
+  int a = 0, b = 0, c = 0, d = 0;
   int rc = read_device_error_fwd(&a, reset != 0);
   if (!rc) rc = read_device_error_fwd2(&c, reset != 0);
   if (!rc) rc = read_device_error_bwd(&b, reset != 0);
-  *out = a ? a : (c ? c : b);
+  if (!rc) rc = read_device_error_dec(&d, reset != 0);
+  *out = a ? a : (c ? c : (b ? b : d));
   return rc;
 }
 int poly_abi_version(void) { return POLY_ABI_VERSION; }
@@ -111,6 +112,22 @@ int poly_pass_fwd(const PolyPassArgs* a, void* stream) {
     case FwdKind::kTc: return launch_pass_fwd_tc(*a, s);
     default: return launch_pass_fwd_simt(*a, s);
   }
+}
+
+int poly_decode_chain(const PolyPassArgs* passes, int n, void* stream) {
+  if (!passes || n < 0) return fail(POLY_EINVAL, "poly_decode_chain: null passes or negative count");
+  for (int i = 0; i < n; ++i) {
+    const int rc = check_pass(&passes[i]);
+    if (rc) return rc;
+    if (passes[i].seq_q != 1 || choose_fwd(passes[i]) != FwdKind::kDecode)
+      return fail(POLY_EUNSUPPORTED, "poly_decode_chain: pass " + std::to_string(i) + " does not take the decode kernel");
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  for (int i = 0; i < n; ++i) {
+    const int rc = launch_pass_decode(passes[i], s, i > 0);
+    if (rc) return rc;
+  }
+  return POLY_OK;
 }
 
 size_t poly_pass_bwd_workspace_size(const PolyPassBwdArgs* a) {

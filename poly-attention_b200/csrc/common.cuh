@@ -69,11 +69,12 @@ size_t pass_bwd_tc_workspace(const PolyPassBwdArgs& a);
 int read_device_error_fwd(int* out, bool reset);
 int read_device_error_bwd(int* out, bool reset);
 int read_device_error_fwd2(int* out, bool reset);
+int read_device_error_dec(int* out, bool reset);
 bool pass_fwd_tc2_eligible(const PolyPassArgs& a);
 int launch_pass_fwd_tc2(const PolyPassArgs& a, cudaStream_t s);
 
 bool pass_decode_eligible(const PolyPassArgs& a);
-int launch_pass_decode(const PolyPassArgs& a, cudaStream_t s);
+int launch_pass_decode(const PolyPassArgs& a, cudaStream_t s, bool dependent = false);
 size_t pass_decode_workspace(const PolyPassArgs& a);
 
 }  // namespace poly

@@ -3,309 +3,524 @@
 // passes over the concatenated cache (poly_attention/poly_attention.py:63-114
 // with cache, n_poly_attention.py:263-313 with cache).
 //
-// Split-K: CTA (split, group) reads keys [split * kps, (split + 1) * kps) of
-// one (batch, kv head) group once and serves all R = heads / kv_heads query
-// heads of the group. A key row (D 16-bit values) is read by D / 8 lanes with
-// 16-byte loads, so a warp covers 32 / (D / 8) keys per step, fully coalesced;
-// values are multiplied by v_mul (the order-n chain's V' = v * msg) and the
-// per-key bias (the previous level's lse) is added on the fly. Each lane group
-// keeps its own running (max, sum, acc) with a lazy max (rescale only when the
-// max grows by more than 2^8); warps write partials that a combine kernel
-// merges, writing out, lse and the optional epilogue product.
+// One launch per pass. The grid is (splits, batch * kv_heads), launched as
+// thread-block clusters of `splits` CTAs along x: the cluster owns one
+// (batch, kv head) group and CTA `split` streams keys [split * kps,
+// (split + 1) * kps) of it exactly once, serving all R = heads / kv_heads
+// query heads of the group.
+//
+// Keys arrive in 64-key stages: a producer warp fills a ring of stages with TMA
+// tensor loads (128-byte swizzle, so ldmatrix reads are free of bank
+// conflicts; rows past seq_k read as zeros) and the 64 per-key bias values with
+// 4-byte cp.async, all completing on the stage's mbarrier. Each of the 4
+// consumer warps takes 16 keys of a stage and computes, on the tensor cores
+// (mma.sync m16n8k16, fp32 accumulation):
+//   S[16 x 16]  = Q[16 x D] . K^T      (rows 0..R-1 are the group's heads,
+//                                       rows R..15 are zero padding)
+//   O[16 x D]  += P[16 x 16] . V'      (P from S's registers, V' = v * v_mul
+//                                       rounded to the storage type, as the
+//                                       order-n chain's v * msg)
+// with an online softmax in the log2 domain (the per-key bias, the previous
+// level's lse, added on the fly; lazy rescale when the running max grows by
+// more than 2^8). The padding rows cost tensor-core issue slots only: with at
+// most 8 real rows per 16 the pass stays HBM-bound by a wide margin, and
+// tcgen05's smallest tile (M = 64) would waste more while adding TMEM round
+// trips. The four warp states are merged through shared memory, then the
+// cluster's CTA records are merged through distributed shared memory, and the
+// cluster writes out, lse and the optional epilogue product: no partials go
+// through HBM and no second kernel runs.
+#include <cooperative_groups.h>
+
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
+#include "tc_host.cuh"
+#include "tc_ptx.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace poly {
 namespace {
 
 constexpr int kWarps = 4;
+constexpr int kWarpKeys = 16;                 // keys per warp per stage (one m16n8k16 K step of P.V)
+constexpr int kTile = kWarps * kWarpKeys;     // keys per stage
+constexpr int kMaxSplits = 8;                 // portable cluster size
+constexpr int kThreads = (kWarps + 1) * 32;  // warps 0..3 consume, warp 4 produces
+
+// Shared memory: ring [stage][array (k, v, v_mul)][64 keys x D] (1024-byte
+// aligned swizzled tiles), bias [stage][64] fp32, full / empty mbarriers and
+// the abort flag. After the key loop the ring holds the merge records.
+template <int D, int NARR>
+__host__ __device__ constexpr int stage_bytes() { return NARR * kTile * D * 2; }
+// ~100 KB of ring per CTA: two CTAs per SM, each with >= one stage in flight
+template <int D, int NARR>
+__host__ __device__ constexpr int num_stages() {
+  return (100 * 1024) / stage_bytes<D, NARR>() < 2   ? 2
+         : (100 * 1024) / stage_bytes<D, NARR>() > 4 ? 4
+                                                      : (100 * 1024) / stage_bytes<D, NARR>();
+}
+template <int D, int R>
+__host__ __device__ constexpr int record_bytes() { return (kWarps + 1) * R * (D + 2) * 4; }
+template <int D, int R, int NARR>
+__host__ __device__ constexpr int ring_bytes() {
+  return num_stages<D, NARR>() * stage_bytes<D, NARR>() > record_bytes<D, R>()
+             ? num_stages<D, NARR>() * stage_bytes<D, NARR>()
+             : record_bytes<D, R>();
+}
+template <int D, int R, int NARR>
+__host__ __device__ constexpr int smem_bytes() {   // + bias, barriers, flag, alignment slack
+  return ring_bytes<D, R, NARR>() + num_stages<D, NARR>() * (kTile * 4 + 16) + 16 + 1024;
+}
+
+static __device__ int g_decode_error = 0;
+
+__device__ __forceinline__ void cp_async4(uint32_t sa, const void* gmem, bool valid) {
+  const int n = valid ? 4 : 0;   // zero-fill past the end
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sa), "l"(gmem), "r"(n) : "memory");
+}
+// arrive on `bar` once this thread's earlier cp.async copies have landed
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = tc::globaltimer();
+  while (!tc::mbar_try_wait(bar, parity))
+    if (tc::globaltimer() - t0 > tc::kWaitNs) return;
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+
+// c[4] += A[16x16] . B[16x8]; A rows 8..15 are zero (a1 = a3 = 0)
+template <typename T>
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+}
 
 template <typename T>
-struct Vec8 {
-  float f[8];
-  __device__ __forceinline__ void load(const T* p) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
-    const T* t = reinterpret_cast<const T*>(&u);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = to_f32(t[e]);
-  }
-};
-
-struct DecodeGeom {
-  int splits, kps;  // key splits and keys per split
-};
-
-template <int D>
-__host__ __device__ constexpr int keys_per_step() { return 32 / (D / 8); }
-
-constexpr int kTileKeys = 32;   // keys per pipeline stage
-constexpr int kStages = 3;
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-  const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  const int n = valid ? 16 : 0;   // zero-fill past the end
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(n) : "memory");
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return tc::pack_bf16(lo, hi);
+  else return tc::pack_f16(lo, hi);
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// elementwise product of two packed pairs, rounded once to T (the product of
+// two 16-bit values is exact in fp32, so this equals fp32 multiply + round)
+template <typename T>
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const __nv_bfloat162 p = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&b));
+    r = *reinterpret_cast<const uint32_t*>(&p);
+  } else {
+    const __half2 p = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    r = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  return r;
+}
+
+// byte offset of 16-byte chunk `ch` of key row `key` inside one stage array:
+// TMA boxes of 64 keys x 64 features (128-byte rows, 128-byte swizzle: chunk
+// c of row r sits at c ^ (r & 7)), one box per 64 features
+__device__ __forceinline__ uint32_t swz(int key, int ch) {
+  return (uint32_t)((ch >> 3) * (kTile * 128) + key * 128 + (((ch & 7) ^ (key & 7)) << 4));
+}
 
 template <typename T, int D, int R, bool HAS_BIAS, bool HAS_VMUL, bool SOFTCLAMP>
-__global__ void __launch_bounds__(kWarps * 32) decode_partial_kernel(const PolyPassArgs a, float* part, int kps) {
-  constexpr int LPK = D / 8;            // lanes per key row (16-byte chunks per row)
-  constexpr int KPS = 32 / LPK;         // keys per warp step
-  constexpr int ROWB = D * 2;           // bytes per row
+__global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_constant__ CUtensorMap tm_k,
+                                                               const __grid_constant__ CUtensorMap tm_v,
+                                                               const __grid_constant__ CUtensorMap tm_m,
+                                                               const PolyPassArgs a, int kps) {
   constexpr int NARR = HAS_VMUL ? 3 : 2;
-  extern __shared__ __align__(16) uint8_t dsm[];
-  uint8_t* st_base = dsm;                                              // [stage][arr][key][ROWB]
-  float* sbias = (float*)(dsm + kStages * NARR * kTileKeys * ROWB);   // [stage][key]
+  constexpr int NST = num_stages<D, NARR>();
+  constexpr int SB = stage_bytes<D, NARR>();
+  constexpr int AB = kTile * D * 2;     // bytes of one array of a stage
+  constexpr int KS = D / 16;            // K steps of Q.K^T
+  constexpr int NB = D / 8;             // n8 column blocks of O
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = dsm_raw + ((1024 - (tc::smem_u32(dsm_raw) & 1023)) & 1023);
+  const uint32_t sbase = tc::smem_u32(dsm);
+  float* sbias = reinterpret_cast<float*>(dsm + ring_bytes<D, R, NARR>());   // [NST][kTile]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbias + NST * kTile);
+  uint64_t* empty = full + NST;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
+  int* err = &g_decode_error;
 
+  cg::cluster_group cluster = cg::this_cluster();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sub = lane / LPK, li = lane % LPK;
   const int group = blockIdx.y;
   const int b = group / a.kv_heads, g = group - b * a.kv_heads;
   const int split = blockIdx.x;
   const int k0 = split * kps, k1 = min(a.seq_k, k0 + kps);
-  const int ntile = (k1 - k0 + kTileKeys - 1) / kTileKeys;
+  const int ntile = k1 > k0 ? (k1 - k0 + kTile - 1) / kTile : 0;
 
-  const T* kg = (const T*)a.k + b * a.k_stride[0] + g * a.k_stride[1];
-  const T* vg = (const T*)a.v + b * a.v_stride[0] + g * a.v_stride[1];
-  const T* mg = HAS_VMUL ? (const T*)a.v_mul + b * a.v_mul_stride[0] + g * a.v_mul_stride[1] : nullptr;
-  const float* bg = HAS_BIAS ? a.bias + b * a.bias_stride[0] + g * a.bias_stride[1] : nullptr;
-
-  auto issue = [&](int tile) {
-    const int stg = tile % kStages;
-    const int kb = k0 + tile * kTileKeys;
-    uint8_t* dst = st_base + stg * NARR * kTileKeys * ROWB;
-    for (int c = threadIdx.x; c < kTileKeys * LPK; c += kWarps * 32) {
-      const int key = c / LPK, ch = c % LPK;
-      const int j = kb + key;
-      const bool ok = j < k1;
-      const int jj = ok ? j : k0;
-      cp_async16(dst + (0 * kTileKeys + key) * ROWB + ch * 16, kg + (int64_t)jj * a.k_stride[2] + ch * 8, ok);
-      cp_async16(dst + (1 * kTileKeys + key) * ROWB + ch * 16, vg + (int64_t)jj * a.v_stride[2] + ch * 8, ok);
-      if (HAS_VMUL)
-        cp_async16(dst + (2 * kTileKeys + key) * ROWB + ch * 16, mg + (int64_t)jj * a.v_mul_stride[2] + ch * 8, ok);
+  // dependents (the next pass of a decode chain) may start as this grid
+  // drains; they wait for this grid before reading anything it writes
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      tc::mbar_init(&full[s], HAS_BIAS ? 33 : 1);   // producer lane 0 (+ tx), + 32 bias lanes
+      tc::mbar_init(&empty[s], kWarps);
     }
-    if (HAS_BIAS && threadIdx.x < kTileKeys) {
-      const int j = kb + threadIdx.x;
-      sbias[stg * kTileKeys + threadIdx.x] = j < k1 ? bg[j] : 0.f;
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+
+  float m = -INFINITY, l = 0.f;   // consumer state of row gq (quad-uniform m)
+  float o[NB][4];
+#pragma unroll
+  for (int n = 0; n < NB; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+  if (warp == kWarps) {
+    // ------------------------------------------------------------ producer
+    const float* bg = HAS_BIAS ? a.bias + b * a.bias_stride[0] + g * a.bias_stride[1] : nullptr;
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&tm_k);
+      tc::tma_prefetch_desc(&tm_v);
+      if (HAS_VMUL) tc::tma_prefetch_desc(&tm_m);
     }
-  };
-
-  float q[R][8];
+    int issued = 0;
+    for (int t = 0; t < ntile; ++t) {
+      const int s = t % NST;
+      if (t >= NST && !tc::mbar_wait_warp(&empty[s], ((t / NST) - 1) & 1, abort_flag, err, 61)) break;
+      const int kb = k0 + t * kTile;
+      // the last key row may come from the previous pass of a decode chain:
+      // wait for that grid first (a no-op without a programmatic dependency)
+      if (kb + kTile >= a.seq_k) asm volatile("griddepcontrol.wait;" ::: "memory");
+      uint8_t* st = dsm + s * SB;
+      if (lane == 0) {
+        tc::mbar_arrive_expect_tx(&full[s], SB);
 #pragma unroll
-  for (int rr = 0; rr < R; ++rr) {
-    Vec8<T> qv;
-    qv.load((const T*)a.q + b * a.q_stride[0] + (g * R + rr) * a.q_stride[1] + li * 8);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) q[rr][e] = qv.f[e] * (SOFTCLAMP ? a.scale : a.scale * kLog2e);
-  }
-  float m[R], l[R], acc[R][8];
-#pragma unroll
-  for (int rr = 0; rr < R; ++rr) {
-    m[rr] = -INFINITY;
-    l[rr] = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[rr][e] = 0.f;
-  }
-  const float sc_in = SOFTCLAMP ? 1.f / a.softclamp : 0.f;
-  const float sc_out = SOFTCLAMP ? a.softclamp * kLog2e : 0.f;
-
-#pragma unroll
-  for (int t = 0; t < kStages - 1; ++t) {
-    if (t < ntile) issue(t);
-    cp_async_commit();
-  }
-  for (int tile = 0; tile < ntile; ++tile) {
-    cp_async_wait<kStages - 2>();
-    __syncthreads();
-    if (tile + kStages - 1 < ntile) issue(tile + kStages - 1);
-    cp_async_commit();
-    const int stg = tile % kStages;
-    const uint8_t* src = st_base + stg * NARR * kTileKeys * ROWB;
-    const int kb = k0 + tile * kTileKeys;
-    // warp w takes keys [w * 8, w * 8 + 8) of the tile, KPS keys per step
-#pragma unroll
-    for (int st = 0; st < kTileKeys / kWarps / KPS; ++st) {
-      const int key = warp * (kTileKeys / kWarps) + st * KPS + sub;
-      const bool valid = kb + key < k1;
-      Vec8<T> kv, vv;
-      kv.load(reinterpret_cast<const T*>(src + (0 * kTileKeys + key) * ROWB + li * 16));
-      vv.load(reinterpret_cast<const T*>(src + (1 * kTileKeys + key) * ROWB + li * 16));
-      if (HAS_VMUL) {
-        Vec8<T> mv;
-        mv.load(reinterpret_cast<const T*>(src + (2 * kTileKeys + key) * ROWB + li * 16));
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vv.f[e] = to_f32(from_f32<T>(vv.f[e] * mv.f[e]));
+        for (int hf = 0; hf < D / 64; ++hf) {
+          tc::tma_load_4d(st + hf * (kTile * 128), &tm_k, &full[s], hf * 64, kb, g, b);
+          tc::tma_load_4d(st + AB + hf * (kTile * 128), &tm_v, &full[s], hf * 64, kb, g, b);
+          if (HAS_VMUL) tc::tma_load_4d(st + 2 * AB + hf * (kTile * 128), &tm_m, &full[s], hf * 64, kb, g, b);
+        }
       }
-      float b2 = 0.f;
       if (HAS_BIAS) {
-        const float braw = sbias[stg * kTileKeys + key];
-        b2 = braw <= kDeadBias ? -INFINITY : braw * kLog2e;
-      }
 #pragma unroll
-      for (int rr = 0; rr < R; ++rr) {
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          s0 = fmaf(q[rr][e], kv.f[e], s0);
-          s1 = fmaf(q[rr][e + 1], kv.f[e + 1], s1);
+        for (int e = 0; e < kTile / 32; ++e) {
+          const int kl = lane + 32 * e, j = kb + kl;
+          cp_async4(tc::smem_u32(sbias + s * kTile + kl), bg + (j < k1 ? j : k0), j < k1);
         }
-        float s = s0 + s1;
-#pragma unroll
-        for (int o = 1; o < LPK; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (SOFTCLAMP) s = tanhf(s * sc_in) * sc_out;
-        s = valid ? s + b2 : -INFINITY;
-        if (s > m[rr] + 8.f) {                  // lazy max: rescale only on large growth
-          const float alpha = exp2f(m[rr] - s);
-          m[rr] = s;
-          l[rr] *= alpha;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[rr][e] *= alpha;
-        }
-        const float pr = (s == -INFINITY) ? 0.f : exp2f(s - m[rr]);
-        l[rr] += pr;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[rr][e] = fmaf(pr, vv.f[e], acc[rr][e]);
+        cp_async_arrive_noinc(&full[s]);
       }
+      issued = t + 1;
+    }
+    if (*abort_flag) {   // let every copy in flight land before the CTA moves on
+      for (int t = max(0, issued - NST); t < issued; ++t) drain_wait(&full[t % NST], (t / NST) & 1);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int gq = lane >> 2, tq = lane & 3;   // mma fragment row group / thread in group
+    // Q as the A operand: row gq (< R) = head g * R + gq, K step ks holds
+    // dims 16 ks + {2 tq, 2 tq + 1} and 16 ks + 8 + {2 tq, 2 tq + 1}
+    uint32_t qa[KS][2];
+    {
+      const T* qrow = (const T*)a.q + b * a.q_stride[0] + (int64_t)(g * R + (gq < R ? gq : 0)) * a.q_stride[1];
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const uint32_t lo = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * tq);
+        const uint32_t hi = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * tq);
+        qa[ks][0] = gq < R ? lo : 0u;
+        qa[ks][1] = gq < R ? hi : 0u;
+      }
+    }
+    const float qk_scale = SOFTCLAMP ? a.scale / a.softclamp : a.scale * kLog2e;
+    const float sc_out = SOFTCLAMP ? a.softclamp * kLog2e : 0.f;
+    const int wk0 = warp * kWarpKeys;
+    for (int tile = 0; tile < ntile; ++tile) {
+      const int s = tile % NST;
+      if (!tc::mbar_wait_warp(&full[s], (tile / NST) & 1, abort_flag, err, 62)) break;
+      const uint32_t sK = sbase + s * SB, sV = sK + AB, sM = sV + AB;
+      const int kb = k0 + tile * kTile;
+
+      // S = Q . K^T for keys wk0 .. wk0 + 15 (two n8 blocks)
+      float sc[2][4];
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+        const int key = wk0 + nb * 8 + (lane & 7);
+#pragma unroll
+        for (int ks = 0; ks < KS; ks += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(sK + swz(key, ks * 2 + (lane >> 3)), b0, b1, b2, b3);
+          mma16816<T>(sc[nb], qa[ks][0], qa[ks][1], b0, b1);
+          mma16816<T>(sc[nb], qa[ks + 1][0], qa[ks + 1][1], b2, b3);
+        }
+      }
+      // scores of row gq, keys wk0 + nb * 8 + 2 tq + e, in the log2 domain
+      float x[4];
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int kl = wk0 + nb * 8 + 2 * tq + e;
+          float v = sc[nb][e] * qk_scale;
+          if (SOFTCLAMP) v = tanhf(v) * sc_out;
+          if (HAS_BIAS) {
+            const float braw = sbias[s * kTile + kl];
+            v = braw <= kDeadBias ? -INFINITY : v + braw * kLog2e;
+          }
+          x[nb * 2 + e] = kb + kl < k1 ? v : -INFINITY;
+        }
+      }
+      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      if (mx > m + 8.f) {   // lazy max: rescale only on large growth (quad-uniform)
+        const float alpha = m == -INFINITY ? 0.f : exp2f(m - mx);
+        m = mx;
+        l *= alpha;
+#pragma unroll
+        for (int n = 0; n < NB; ++n) {
+          o[n][0] *= alpha;
+          o[n][1] *= alpha;
+        }
+      }
+      float p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) p[e] = x[e] == -INFINITY ? 0.f : exp2f(x[e] - m);
+      l += (p[0] + p[1]) + (p[2] + p[3]);
+      const uint32_t pa0 = pack2<T>(p[0], p[1]), pa2 = pack2<T>(p[2], p[3]);
+
+      // O += P . V' : ldmatrix.trans gives V' as the B operand (keys x dims)
+      const int vkey = wk0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int n2 = 0; n2 < NB / 2; ++n2) {
+        const uint32_t off = swz(vkey, n2 * 2 + (lane >> 4));
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(sV + off, v0, v1, v2, v3);
+        if (HAS_VMUL) {
+          uint32_t m0, m1, m2, m3;
+          ldsm_x4_t(sM + off, m0, m1, m2, m3);
+          v0 = mul2<T>(v0, m0);
+          v1 = mul2<T>(v1, m1);
+          v2 = mul2<T>(v2, m2);
+          v3 = mul2<T>(v3, m3);
+        }
+        mma16816<T>(o[2 * n2], pa0, pa2, v0, v1);
+        mma16816<T>(o[2 * n2 + 1], pa0, pa2, v2, v3);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty[s]);
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+  }
+  __syncthreads();   // the ring is idle (every issued stage consumed or drained): reuse it
+
+  // warp records [warp][row][m, l, acc[D]], then the CTA record [row][...]
+  float* wrec = reinterpret_cast<float*>(dsm);
+  float* crec = wrec + kWarps * R * (D + 2);
+  if (warp < kWarps && (lane >> 2) < R) {
+    const int gq = lane >> 2, tq = lane & 3;
+    float* r = wrec + (warp * R + gq) * (D + 2);
+#pragma unroll
+    for (int n = 0; n < NB; ++n) {
+      r[2 + n * 8 + 2 * tq] = o[n][0];
+      r[2 + n * 8 + 2 * tq + 1] = o[n][1];
+    }
+    if (tq == 0) {
+      r[0] = m;
+      r[1] = l;
     }
   }
-  cp_async_wait<0>();
-  // merge the KPS lane groups of this warp (lanes li, li + LPK, ...)
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < R * D; idx += kThreads) {
+    const int rr = idx / D, c = idx - rr * D;
+    float M = -INFINITY;
 #pragma unroll
-  for (int rr = 0; rr < R; ++rr) {
-    float mm = m[rr];
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wrec[(w * R + rr) * (D + 2)]);
+    float acc = 0.f, ls = 0.f;
 #pragma unroll
-    for (int o = LPK; o < 32; o <<= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
-    const float f = (mm == -INFINITY) ? 0.f : exp2f(m[rr] - mm);
-    float ll = l[rr] * f;
-#pragma unroll
-    for (int o = LPK; o < 32; o <<= 1) ll += __shfl_xor_sync(0xffffffffu, ll, o);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float x = acc[rr][e] * f;
-#pragma unroll
-      for (int o = LPK; o < 32; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-      acc[rr][e] = x;
+    for (int w = 0; w < kWarps; ++w) {
+      const float* r = wrec + (w * R + rr) * (D + 2);
+      const float f = r[0] == -INFINITY ? 0.f : exp2f(r[0] - M);
+      acc = fmaf(r[2 + c], f, acc);
+      ls = fmaf(r[1], f, ls);
     }
-    // partial record: [m, l, acc[D]] per (group, split * kWarps + warp, rr)
-    float* rec = part + (((int64_t)group * gridDim.x * kWarps + split * kWarps + warp) * R + rr) * (D + 2);
-    if (sub == 0) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) rec[2 + li * 8 + e] = acc[rr][e];
-      if (li == 0) {
-        rec[0] = mm;
-        rec[1] = ll;
-      }
+    crec[rr * (D + 2) + 2 + c] = acc;
+    if (c == 0) {
+      crec[rr * (D + 2)] = M;
+      crec[rr * (D + 2) + 1] = ls;
     }
   }
+  cluster.sync();   // CTA records visible to the whole cluster
+
+  // cluster merge: CTA `split` writes its share of the group's R x D outputs
+  const int nsp = gridDim.x;
+  for (int idx = split * kThreads + threadIdx.x; idx < R * D; idx += nsp * kThreads) {
+    const int rr = idx / D, c = idx - rr * D;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsp; ++sp) M = fmaxf(M, cluster.map_shared_rank(crec, sp)[rr * (D + 2)]);
+    float acc = 0.f, L = 0.f;
+    for (int sp = 0; sp < nsp; ++sp) {
+      const float* r = cluster.map_shared_rank(crec, sp) + rr * (D + 2);
+      const float ms = r[0];
+      const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
+      acc = fmaf(r[2 + c], f, acc);
+      L = fmaf(r[1], f, L);
+    }
+    const int h = g * R + rr;
+    const T ov = from_f32<T>(L > 0.f ? acc / L : 0.f);
+    ((T*)a.out)[b * a.out_stride[0] + h * a.out_stride[1] + c] = ov;
+    if (a.epi_out) {
+      const T em = ((const T*)a.epi_mul)[b * a.epi_mul_stride[0] + h * a.epi_mul_stride[1] + c];
+      ((T*)a.epi_out)[b * a.epi_out_stride[0] + h * a.epi_out_stride[1] + c] = from_f32<T>(to_f32(em) * to_f32(ov));
+    }
+    if (a.lse && c == 0) a.lse[b * a.lse_stride[0] + h * a.lse_stride[1]] = (M + __log2f(L)) * kLn2;
+  }
+  cluster.sync();   // no CTA leaves while its record may still be read
 }
 
-// One warp per (group, head-in-group): merge all partials of the row. Lanes
-// read the (max, sum) of different partials in parallel; the accumulators are
-// then summed with independent loads.
-template <typename T, int D, int R>
-__global__ void decode_combine_kernel(const PolyPassArgs a, const float* part, int nparts) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const int groups = a.batch * a.kv_heads;
-  if (w >= groups * R) return;
-  const int group = w / R, rr = w - group * R;
-  const int b = group / a.kv_heads, g = group - b * a.kv_heads, h = g * R + rr;
-  auto rec = [&](int pi) { return part + (((int64_t)group * nparts + pi) * R + rr) * (D + 2); };
-  // lane p owns partials p and p + 32 (nparts <= 64): their weights stay in
-  // registers and are broadcast with shuffles, so every accumulator load below
-  // is independent of the others
-  float mv0 = -INFINITY, mv1 = -INFINITY, lv0 = 0.f, lv1 = 0.f;
-  if (lane < nparts) { mv0 = rec(lane)[0]; lv0 = rec(lane)[1]; }
-  if (lane + 32 < nparts) { mv1 = rec(lane + 32)[0]; lv1 = rec(lane + 32)[1]; }
-  const float M = warp_max(fmaxf(mv0, mv1));
-  const float w0 = (mv0 == -INFINITY) ? 0.f : exp2f(mv0 - M);
-  const float w1 = (mv1 == -INFINITY) ? 0.f : exp2f(mv1 - M);
-  const float L = warp_sum(lv0 * w0 + lv1 * w1);
-  float o[D / 32];
-#pragma unroll
-  for (int t = 0; t < D / 32; ++t) o[t] = 0.f;
-#pragma unroll 8
-  for (int pi = 0; pi < nparts; ++pi) {
-    const float f = __shfl_sync(0xffffffffu, pi < 32 ? w0 : w1, pi & 31);
-    const float* r_ = rec(pi);
-#pragma unroll
-    for (int t = 0; t < D / 32; ++t) o[t] = fmaf(r_[2 + lane + 32 * t], f, o[t]);
+}  // namespace
+
+int read_device_error_dec(int* out, bool reset) {
+  int rc = cuda_status(cudaMemcpyFromSymbol(out, g_decode_error, sizeof(int)), "read device error word");
+  if (rc == POLY_OK && reset) {
+    const int zero = 0;
+    rc = cuda_status(cudaMemcpyToSymbol(g_decode_error, &zero, sizeof(int)), "reset device error word");
   }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  T* out = (T*)a.out + b * a.out_stride[0] + h * a.out_stride[1];
-  const T* em = a.epi_out ? (const T*)a.epi_mul + b * a.epi_mul_stride[0] + h * a.epi_mul_stride[1] : nullptr;
-  T* eo = a.epi_out ? (T*)a.epi_out + b * a.epi_out_stride[0] + h * a.epi_out_stride[1] : nullptr;
-#pragma unroll
-  for (int t = 0; t < D / 32; ++t) {
-    const T ov = from_f32<T>(o[t] * inv);
-    out[lane + 32 * t] = ov;
-    if (eo) eo[lane + 32 * t] = from_f32<T>(to_f32(em[lane + 32 * t]) * to_f32(ov));
-  }
-  if (a.lse && lane == 0) a.lse[b * a.lse_stride[0] + h * a.lse_stride[1]] = (M + __log2f(L)) * kLn2;
+  return rc;
 }
 
-DecodeGeom geometry(const PolyPassArgs& a, int keys_step) {
+namespace {
+
+struct DecodeGeom {
+  int splits, kps;  // key splits (cluster size) and keys per split
+};
+
+// Splits per group: the most (<= kMaxSplits) that still fit every CTA of the
+// grid into one wave (`slots` = resident CTAs per SM x SMs), so that each CTA
+// streams one long key range and pays its pipeline ramp-up and merge once;
+// at least one 64-key tile per split. POLY_DECODE_SPLITS overrides (tuning).
+DecodeGeom geometry(const PolyPassArgs& a, int slots) {
   const int groups = a.batch * a.kv_heads;
-  const int step = kTileKeys;                 // keys one CTA stages per pipeline step
-  (void)keys_step;
-  int splits = (a.seq_k + step - 1) / step;                       // at most one warp-step of keys per warp
-  const int want = (8 * 148 + groups - 1) / groups;               // ~8 CTAs per SM
-  splits = max(1, min(min(splits, want), 64 / kWarps));   // the combine holds <= 64 partials per row
+  const int ntiles = (a.seq_k + kTile - 1) / kTile;
+  int splits = max(1, min(kMaxSplits, slots / max(groups, 1)));
+  static const int forced = [] {
+    const char* e = getenv("POLY_DECODE_SPLITS");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced > 0) splits = min(forced, kMaxSplits);
+  splits = max(1, min(splits, ntiles));
   DecodeGeom gm;
-  gm.kps = (a.seq_k + splits - 1) / splits;
-  gm.kps = (gm.kps + step - 1) / step * step;
-  gm.splits = (a.seq_k + gm.kps - 1) / gm.kps;
+  gm.kps = max(kTile, ((a.seq_k + splits - 1) / splits + kTile - 1) / kTile * kTile);
+  gm.splits = max(1, (a.seq_k + gm.kps - 1) / gm.kps);
   return gm;
 }
 
-template <int D, bool V>
-constexpr int smem_bytes() { return kStages * (V ? 3 : 2) * kTileKeys * D * 2 + kStages * kTileKeys * 4; }
+// (batch, kv head, row) strides for a tensor map: the stride of an extent-1
+// dimension is never used, so it is replaced by one TMA accepts
+void map_strides(const int64_t* st, const PolyPassArgs& a, int64_t* out) {
+  out[2] = st[2] > 0 ? st[2] : a.head_dim;
+  out[1] = (a.kv_heads == 1 || st[1] <= 0) ? out[2] * max(a.seq_k, 1) : st[1];
+  out[0] = (a.batch == 1 || st[0] <= 0) ? out[1] * a.kv_heads : st[0];
+}
+
+template <typename T, int D, int R, bool B, bool V, bool C>
+int launch_one(const PolyPassArgs& a, cudaStream_t s, bool dependent) {
+  constexpr int smem = smem_bytes<D, R, V ? 3 : 2>();
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(decode_split_kernel<T, D, R, B, V, C>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  if (attr_err != cudaSuccess) return cuda_status(attr_err, "cudaFuncSetAttribute(decode)");
+  // resident CTAs per SM x SMs of the current device (cached per device)
+  static std::mutex mu;
+  static int slots_dev[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  int slots;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!slots_dev[dev]) {
+      int per_sm = 0, sms = 0;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_split_kernel<T, D, R, B, V, C>, kThreads, smem);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      slots_dev[dev] = max(1, per_sm) * max(1, sms);
+    }
+    slots = slots_dev[dev];
+  }
+  const DecodeGeom gm = geometry(a, slots);
+  CUtensorMap tk, tv, tm;
+  const int rows = max(a.seq_k, 1);   // seq_k == 0 issues no load
+  int64_t ks[3], vs[3], ms[3];
+  map_strides(a.k_stride, a, ks);
+  map_strides(a.v_stride, a, vs);
+  int rc = make_map(&tk, a.k, a.dtype, D, rows, a.kv_heads, a.batch, ks, kTile);
+  if (!rc) rc = make_map(&tv, a.v, a.dtype, D, rows, a.kv_heads, a.batch, vs, kTile);
+  memset(&tm, 0, sizeof(tm));
+  if (!rc && V) {
+    map_strides(a.v_mul_stride, a, ms);
+    rc = make_map(&tm, a.v_mul, a.dtype, D, rows, a.kv_heads, a.batch, ms, kTile);
+  }
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(gm.splits, a.batch * a.kv_heads);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = gm.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = dependent ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<T, D, R, B, V, C>, tk, tv, tm, a, gm.kps);
+  note_launch(1);
+  return cuda_status(e, "decode launch");
+}
 
 template <typename T, int D, int R>
-int launch3(const PolyPassArgs& a, cudaStream_t s) {
-  const DecodeGeom gm = geometry(a, keys_per_step<D>());
-  float* part = (float*)a.workspace;
-  dim3 grid(gm.splits, a.batch * a.kv_heads);
+int launch3(const PolyPassArgs& a, cudaStream_t s, bool dep) {
   const bool bias = a.bias != nullptr, vm = a.v_mul != nullptr, sc = a.softclamp > 0.f;
-#define POLY_DEC(B, V, C)                                                                                  \
-  do {                                                                                                     \
-    static std::once_flag once_;                                                                           \
-    static cudaError_t err_ = cudaSuccess;                                                                 \
-    std::call_once(once_, [] {                                                                             \
-      err_ = cudaFuncSetAttribute(decode_partial_kernel<T, D, R, B, V, C>,                                 \
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<D, V>());        \
-    });                                                                                                    \
-    if (err_ != cudaSuccess) return cuda_status(err_, "cudaFuncSetAttribute(decode)");                     \
-    decode_partial_kernel<T, D, R, B, V, C><<<grid, kWarps * 32, smem_bytes<D, V>(), s>>>(a, part, gm.kps); \
-  } while (0)
   if (sc) {
-    if (bias) { if (vm) POLY_DEC(true, true, true); else POLY_DEC(true, false, true); }
-    else { if (vm) POLY_DEC(false, true, true); else POLY_DEC(false, false, true); }
-  } else {
-    if (bias) { if (vm) POLY_DEC(true, true, false); else POLY_DEC(true, false, false); }
-    else { if (vm) POLY_DEC(false, true, false); else POLY_DEC(false, false, false); }
+    if (bias) return vm ? launch_one<T, D, R, true, true, true>(a, s, dep) : launch_one<T, D, R, true, false, true>(a, s, dep);
+    return vm ? launch_one<T, D, R, false, true, true>(a, s, dep) : launch_one<T, D, R, false, false, true>(a, s, dep);
   }
-#undef POLY_DEC
-  const int rows = a.batch * a.kv_heads * R;
-  decode_combine_kernel<T, D, R><<<(rows * 32 + 255) / 256, 256, 0, s>>>(a, part, gm.splits * kWarps);
-  note_launch(2);
-  return cuda_status(cudaGetLastError(), "decode launch");
+  if (bias) return vm ? launch_one<T, D, R, true, true, false>(a, s, dep) : launch_one<T, D, R, true, false, false>(a, s, dep);
+  return vm ? launch_one<T, D, R, false, true, false>(a, s, dep) : launch_one<T, D, R, false, false, false>(a, s, dep);
 }
 
 template <typename T, int D>
-int launch2(const PolyPassArgs& a, cudaStream_t s) {
+int launch2(const PolyPassArgs& a, cudaStream_t s, bool dep) {
   switch (a.heads / a.kv_heads) {
-    case 1: return launch3<T, D, 1>(a, s);
-    case 2: return launch3<T, D, 2>(a, s);
-    case 4: return launch3<T, D, 4>(a, s);
-    default: return launch3<T, D, 8>(a, s);
+    case 1: return launch3<T, D, 1>(a, s, dep);
+    case 2: return launch3<T, D, 2>(a, s, dep);
+    case 4: return launch3<T, D, 4>(a, s, dep);
+    default: return launch3<T, D, 8>(a, s, dep);
   }
 }
-
-bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 }  // namespace
 
@@ -320,18 +535,22 @@ bool pass_decode_eligible(const PolyPassArgs& a) {
   if ((a.k_stride[0] | a.k_stride[1] | a.v_stride[0] | a.v_stride[1]) & 7) return false;
   if (a.v_mul && (!aligned16(a.v_mul) || ((a.v_mul_stride[0] | a.v_mul_stride[1] | a.v_mul_stride[2]) & 7)))
     return false;
+  // TMA needs positive strides wherever the extent exceeds one
+  auto pos = [&](const int64_t* st) {
+    return (a.seq_k <= 1 || st[2] > 0) && (a.kv_heads == 1 || st[1] > 0) && (a.batch == 1 || st[0] > 0);
+  };
+  if (!pos(a.k_stride) || !pos(a.v_stride) || (a.v_mul && !pos(a.v_mul_stride))) return false;
   return true;
 }
 
-size_t pass_decode_workspace(const PolyPassArgs& a) {
-  const DecodeGeom gm = geometry(a, a.head_dim == 64 ? keys_per_step<64>() : keys_per_step<128>());
-  return (size_t)a.batch * a.kv_heads * gm.splits * kWarps * (a.heads / a.kv_heads) * (a.head_dim + 2) * sizeof(float);
-}
+// partials never leave the cluster: no workspace
+size_t pass_decode_workspace(const PolyPassArgs&) { return 0; }
 
-int launch_pass_decode(const PolyPassArgs& a, cudaStream_t s) {
+int launch_pass_decode(const PolyPassArgs& a, cudaStream_t s, bool dependent) {
   if (a.dtype == POLY_BF16)
-    return a.head_dim == 64 ? launch2<__nv_bfloat16, 64>(a, s) : launch2<__nv_bfloat16, 128>(a, s);
-  return a.head_dim == 64 ? launch2<__half, 64>(a, s) : launch2<__half, 128>(a, s);
+    return a.head_dim == 64 ? launch2<__nv_bfloat16, 64>(a, s, dependent)
+                            : launch2<__nv_bfloat16, 128>(a, s, dependent);
+  return a.head_dim == 64 ? launch2<__half, 64>(a, s, dependent) : launch2<__half, 128>(a, s, dependent);
 }
 
 }  // namespace poly

@@ -66,6 +66,7 @@ EXPORTS = {
     "poly_pass_bwd": (ctypes.c_int, [ctypes.POINTER(PolyPassBwdArgs), c_vp]),
     "poly_pass_bwd_workspace_size": (c_sz, [ctypes.POINTER(PolyPassBwdArgs)]),
     "poly_lse_merge": (ctypes.c_int, [ctypes.POINTER(PolyMergeArgs), c_vp]),
+    "poly_decode_chain": (ctypes.c_int, [ctypes.POINTER(PolyPassArgs), ctypes.c_int, c_vp]),
     "poly_pass_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(PolyPassBwdArgs), c_vp]),
     "poly_noalloc_scratch_bytes": (c_sz, []),
     "poly_pass_fwd_kernel_name": (ctypes.c_char_p, [ctypes.POINTER(PolyPassArgs)]),

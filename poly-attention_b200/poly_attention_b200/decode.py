@@ -4,10 +4,14 @@ The reference grows its cache with ``torch.cat`` every step
 (poly_attention/poly_attention.py:283-287, n_poly_attention.py:206-207,
 281-302), copying the whole cache each time. ``ChainDecoder`` keeps the same
 cache contents in buffers allocated once with a fixed capacity and appends
-each new row in place; every level of the chain is one call of the decode
-kernel (``poly_pass_fwd`` with seq_q == 1) whose output row is written
-straight into the level's msg / lse cache. Per-level argument blocks are
-built once and only their length and row pointers change per step.
+each new row in place. A step is one ``poly_decode_chain`` call: one decode
+kernel per level (seq_q == 1), each writing its output row straight into the
+level's msg / lse cache, launched as programmatic dependents so that a level
+streams its cache while the previous level drains (a level reads the
+previous level's output only in the appended row, the chain's contract).
+Dtypes / sizes the decode kernel does not take run level by level through
+``poly_pass_fwd``. The argument blocks live in one array built once; only the
+length and the row pointers change per step.
 
 Cache layout (kv-head width, as the kernels read it):
   qs[t]   [b, g, cap, d]  for t = 0 .. order-1  (q2 .. q_{order+1})
@@ -45,11 +49,14 @@ class ChainDecoder:
                      for _ in range(order - 1)]
         self.length = 0
         self._stream = None
-        # one argument block per level t = order-1 .. 0 (level t: queries q_{t+1}, keys q_{t+2})
+        # one argument block per level t = order-1 .. 0 (level t: queries q_{t+1}, keys q_{t+2}),
+        # in launch order in one array (element order-1-t is level t)
+        self._arr = (PolyPassArgs * order)()
         self._args = {}
         self._ws = {}
+        self._chain = None           # poly_decode_chain usable (decided on the first step)
         for t in range(order - 1, -1, -1):
-            a = PolyPassArgs()
+            a = self._arr[order - 1 - t]
             a.batch, a.kv_heads, a.head_dim = batch, kv_heads, dim_head
             a.heads = heads if t == 0 else kv_heads
             a.seq_q = 1
@@ -117,6 +124,17 @@ class ChainDecoder:
                 a.q, a.q_stride = q1_new.data_ptr(), _st3(q1_new)
                 a.out, a.out_stride = out.data_ptr(), _st3(out)
                 a.lse = None
+        if self._chain is not False:
+            rc = lib.poly_decode_chain(self._arr, self.order, stream)
+            if rc == _lib.POLY_OK:
+                self._chain = True
+                self.length = n
+                return out
+            if rc != _lib.POLY_EUNSUPPORTED or self._chain:
+                check(rc, "poly_decode_chain")
+            self._chain = False
+        for t in range(self.order - 1, -1, -1):
+            a = self._args[t]
             self._workspace(t, a)
             check(lib.poly_pass_fwd(ctypes.byref(a), stream), "poly_pass_fwd (decode)")
         self.length = n

@@ -50,6 +50,11 @@ def test_invalid_args_report_errors_without_gpu():
     assert "divisible" in _lib.lib.poly_last_error().decode()
     a.heads, a.head_dim = 2, 512
     assert _lib.lib.poly_pass_fwd(ctypes.byref(a), None) == _lib.POLY_EUNSUPPORTED
+    # poly_decode_chain validates every pass before launching any
+    assert _lib.lib.poly_decode_chain(None, 1, None) == _lib.POLY_EINVAL
+    assert _lib.lib.poly_decode_chain(ctypes.byref(a), -1, None) == _lib.POLY_EINVAL
+    assert _lib.lib.poly_decode_chain(ctypes.byref(a), 0, None) == _lib.POLY_OK
+    assert _lib.lib.poly_decode_chain(ctypes.byref(a), 1, None) == _lib.POLY_EUNSUPPORTED
 
 
 def test_product_path_refuses_cpu_tensors():

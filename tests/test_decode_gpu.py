@@ -24,7 +24,7 @@ def host(t):
 
 
 @pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("h,g", [(4, 4), (16, 4), (8, 1)])
+@pytest.mark.parametrize("h,g", [(4, 4), (16, 4), (8, 4), (8, 1)])
 @pytest.mark.parametrize("L", [1, 37, 2049])
 @pytest.mark.parametrize("extras", ["none", "bias", "bias+vmul+epi"])
 def test_decode_pass(d, h, g, L, extras):
@@ -55,6 +55,29 @@ def test_decode_pass(d, h, g, L, extras):
     np.testing.assert_allclose(host(lse), el, atol=ATOL, rtol=RTOL)
     if "epi" in extras:
         np.testing.assert_allclose(host(eo), em * host(out), atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("d,h,g,L", [(64, 8, 4, 300), (128, 16, 2, 20000), (128, 4, 4, 65), (64, 2, 1, 4096)])
+def test_decode_pass_softclamp_dead_keys(dt, d, h, g, L):
+    """Softclamp, fp16, GQA ratios 2 and 8, long caches (the largest split
+    count) and dead keys (bias <= -FLT_MAX / 2, the previous level's lse of a
+    fully masked row) together."""
+    import poly_attention_b200 as P
+    b = 2
+    q = host(dev(rnd((b, h, 1, d), 11), dt))
+    k, v, vm = (host(dev(rnd((b, g, L, d), s), dt)) for s in (12, 13, 14))
+    bias = rnd((b, g, L), 15)
+    bias[:, :, ::7] = -np.finfo(np.float32).max
+    vv = host(dev(v * vm, dt))
+    qt, kt, vt = dev(q, dt), dev(k, dt), dev(v, dt)
+    assert P.kernel_names(qt, kt, vt)[0] == "decode"
+    out, lse = P.pass_fwd(qt, kt, vt, softclamp=10.0, bias=dev(bias, torch.float32), v_mul=dev(vm, dt))
+    r = h // g
+    eo_, el = O.pass_fwd(q, np.repeat(k, r, 1), np.repeat(vv, r, 1), softclamp_value=10.0,
+                         bias=np.repeat(bias, r, 1))
+    np.testing.assert_allclose(host(out), eo_, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(host(lse), el, atol=ATOL, rtol=RTOL)
 
 
 @pytest.mark.parametrize("order,d", [(2, 64), (3, 128)])
@@ -106,3 +129,35 @@ def test_chain_decoder_matches_parallel_oracle(order, d, h, g):
     ref, _, _ = O.npoly_chain_fwd([q1] + [rep(x) for x in qs[:-1]], [rep(x) for x in qs], [rep(x) for x in vs],
                                   causal=True)
     np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("order,d,h,g,L0", [(3, 128, 16, 4, 3000), (4, 64, 8, 2, 700)])
+def test_decode_chain_equals_level_by_level(order, d, h, g, L0):
+    """One poly_decode_chain call per step (levels launched as programmatic
+    dependents, each streaming its cache before waiting for the previous
+    level) gives bit-identical results to the same kernels launched level by
+    level with full stream serialisation, over many steps of long caches."""
+    from poly_attention_b200.decode import ChainDecoder
+    dt = torch.bfloat16
+    b, steps = 4, 24
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    decs = [ChainDecoder(batch=b, order=order, heads=h, kv_heads=g, dim_head=d, capacity=L0 + steps + 8, dtype=dt)
+            for _ in range(2)]
+    for bufs in zip(*[dd.qs + dd.vs + dd.msgs + dd.lses for dd in decs]):
+        bufs[0][:, :, :L0].normal_(generator=gen)
+        bufs[1].copy_(bufs[0])
+    for dd in decs:
+        dd.length = L0
+    decs[1]._chain = False
+    for i in range(steps):
+        qn = [torch.randn(b, g, 1, d, device="cuda", dtype=dt, generator=gen) for _ in range(order)]
+        vn = [torch.randn(b, g, 1, d, device="cuda", dtype=dt, generator=gen) for _ in range(order - 1)]
+        q1 = torch.randn(b, h, 1, d, device="cuda", dtype=dt, generator=gen)
+        outs = []
+        for dd in decs:
+            dd.append_kv(qn, vn)
+            outs.append(dd.step(q1).clone())
+        assert torch.equal(outs[0], outs[1]), f"step {i}"
+    assert decs[0]._chain is True
+    for m0, m1 in zip(decs[0].msgs + decs[0].lses, decs[1].msgs + decs[1].lses):
+        assert torch.equal(m0[:, :, :L0 + steps], m1[:, :, :L0 + steps])
