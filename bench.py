@@ -164,13 +164,21 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
 
-    # end to end through the public API: host (pinned) inputs in, gradients out
+    # end to end through the public API: host (pinned) inputs in, gradients out.
+    # Headline: HostStreamedOrder2 (batch chunks streamed, PCIe both ways
+    # overlapped with the kernels); also the plain autograd call
+    # (flash_poly_attention + backward, copies before and after).
     e2e = None
     if not args.no_e2e:
         hosts = [x.cpu().pin_memory() for x in (q1, q2, q3, v3, do)]
         grads_h = [torch.empty_like(hosts[0]).pin_memory() for _ in range(4)]
+        streamer = P.HostStreamedOrder2(batch=b, heads=H, kv_heads=H, seq_len=N, dim_head=D, device=dev,
+                                        chunk=args.e2e_chunk)
 
-        def e2e_step():
+        def e2e_streamed():
+            streamer.step(*hosts, grads=grads_h)
+
+        def e2e_autograd():
             d_in = [h.to(dev, non_blocking=True) for h in hosts]
             ts = [x.requires_grad_(True) for x in d_in[:4]]
             out = P.flash_poly_attention(*ts, is_causal=True)
@@ -178,23 +186,28 @@ def run_ours(args, rank, world, local_rank):
             for gh, tt in zip(grads_h, ts):
                 gh.copy_(tt.grad, non_blocking=True)
 
-        e2e_step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        k2 = max(1, min(args.steps, 5))
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record()
-        for _ in range(k2):
-            e2e_step()
-        e2.record()
-        torch.cuda.synchronize()
-        te = torch.tensor([s2.elapsed_time(e2) / k2], device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": b * N * world / (float(te.item()) * 1e-3), "unit": "tokens/s",
-               "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h in hosts),
-               "d2h_bytes_per_step": sum(g.numel() * g.element_size() for g in grads_h)}
+        def timed(fn):
+            fn()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            k2 = max(1, min(args.steps, 5))
+            s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s2.record()
+            for _ in range(k2):
+                fn()
+            e2.record()
+            torch.cuda.synchronize()
+            te = torch.tensor([s2.elapsed_time(e2) / k2], device=dev)
+            if world > 1:
+                dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            return b * N * world / (float(te.item()) * 1e-3)
+
+        h2d, d2h = streamer.bytes_per_step()
+        e2e = {"value": timed(e2e_streamed), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "api": f"HostStreamedOrder2.step (chunk {args.e2e_chunk})",
+               "autograd_serial": {"value": timed(e2e_autograd), "unit": "tokens/s",
+                                   "api": "flash_poly_attention + backward, copies before / after"}}
     decode = None if args.no_decode else run_decode(args, dev)
     if world > 1:
         dist.barrier()
@@ -443,6 +456,7 @@ def main():
     ap.add_argument("--batch", type=int, default=B, help="per-GPU batch (smaller for profiling captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--e2e-chunk", type=int, default=1, help="batch elements per streamed chunk (e2e leg)")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
     ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4", "decode"], default="train",
                     help="train: config 2 fwd+bwd (the headline); longctx: config 5 key-split forward")
