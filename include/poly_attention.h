@@ -173,6 +173,29 @@ POLY_API int poly_lse_merge(const PolyMergeArgs* args, void* stream);
 POLY_API int poly_decode_chain(const PolyPassArgs* passes, int n, void* stream);
 
 /*
+ * Row copies for KV-cache appends (replaces the reference's per-step
+ * torch.cat cache growth, poly_attention/poly_attention.py:283-287 and
+ * n_poly_attention.py:206-207, 281-302, by in-place writes of the new rows).
+ * Copy i moves outer x inner rows of row_bytes bytes; row (o, i) starts at
+ * src + o * src_stride[0] + i * src_stride[1] (same for dst). All n <= 16
+ * copies run in ONE kernel launch. Pointers, strides and row_bytes must be
+ * multiples of 16 bytes, else POLY_EINVAL.
+ */
+#define POLY_MAX_ROW_COPIES 16
+typedef struct {
+  const void* src;
+  void* dst;
+  int32_t outer;
+  int32_t inner;
+  int32_t row_bytes;
+  int32_t reserved;
+  int64_t src_stride[2]; /* bytes */
+  int64_t dst_stride[2]; /* bytes */
+} PolyRowCopy;
+
+POLY_API int poly_copy_rows(const PolyRowCopy* copies, int n, void* stream);
+
+/*
  * poly_pass_bwd without a caller workspace. No counterpart in the reference:
  * it exists for callers that cannot allocate device memory (FFI hosts that
  * only pass existing buffers, processes whose device memory another

@@ -114,6 +114,10 @@ int poly_pass_fwd(const PolyPassArgs* a, void* stream) {
   }
 }
 
+int poly_copy_rows(const PolyRowCopy* copies, int n, void* stream) {
+  return copy_rows(copies, n, (cudaStream_t)stream);
+}
+
 int poly_decode_chain(const PolyPassArgs* passes, int n, void* stream) {
   if (!passes || n < 0) return fail(POLY_EINVAL, "poly_decode_chain: null passes or negative count");
   for (int i = 0; i < n; ++i) {

@@ -76,5 +76,6 @@ int launch_pass_fwd_tc2(const PolyPassArgs& a, cudaStream_t s);
 bool pass_decode_eligible(const PolyPassArgs& a);
 int launch_pass_decode(const PolyPassArgs& a, cudaStream_t s, bool dependent = false);
 size_t pass_decode_workspace(const PolyPassArgs& a);
+int copy_rows(const PolyRowCopy* copies, int n, cudaStream_t s);
 
 }  // namespace poly

@@ -60,6 +60,14 @@ class PolyMergeArgs(ctypes.Structure):
     ]
 
 
+class PolyRowCopy(ctypes.Structure):
+    _fields_ = [("src", c_vp), ("dst", c_vp), ("outer", ctypes.c_int32), ("inner", ctypes.c_int32),
+                ("row_bytes", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("src_stride", ctypes.c_int64 * 2), ("dst_stride", ctypes.c_int64 * 2)]
+
+
+MAX_ROW_COPIES = 16
+
 EXPORTS = {
     "poly_pass_fwd": (ctypes.c_int, [ctypes.POINTER(PolyPassArgs), c_vp]),
     "poly_pass_fwd_workspace_size": (c_sz, [ctypes.POINTER(PolyPassArgs)]),
@@ -67,6 +75,7 @@ EXPORTS = {
     "poly_pass_bwd_workspace_size": (c_sz, [ctypes.POINTER(PolyPassBwdArgs)]),
     "poly_lse_merge": (ctypes.c_int, [ctypes.POINTER(PolyMergeArgs), c_vp]),
     "poly_decode_chain": (ctypes.c_int, [ctypes.POINTER(PolyPassArgs), ctypes.c_int, c_vp]),
+    "poly_copy_rows": (ctypes.c_int, [ctypes.POINTER(PolyRowCopy), ctypes.c_int, c_vp]),
     "poly_pass_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(PolyPassBwdArgs), c_vp]),
     "poly_noalloc_scratch_bytes": (c_sz, []),
     "poly_pass_fwd_kernel_name": (ctypes.c_char_p, [ctypes.POINTER(PolyPassArgs)]),

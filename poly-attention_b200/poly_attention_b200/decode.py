@@ -49,6 +49,13 @@ class ChainDecoder:
                      for _ in range(order - 1)]
         self.length = 0
         self._stream = None
+        # row copies of append_kv: one per key / value cache, fixed shape and strides
+        nb = len(self.qs) + len(self.vs)
+        self._copies = (_lib.PolyRowCopy * max(nb, 1))()
+        for c, buf in zip(self._copies, self.qs + self.vs):
+            esz = buf.element_size()
+            c.outer, c.inner, c.row_bytes = batch, kv_heads, dim_head * esz
+            c.dst_stride[0], c.dst_stride[1] = buf.stride(0) * esz, buf.stride(1) * esz
         # one argument block per level t = order-1 .. 0 (level t: queries q_{t+1}, keys q_{t+2}),
         # in launch order in one array (element order-1-t is level t)
         self._arr = (PolyPassArgs * order)()
@@ -100,8 +107,19 @@ class ChainDecoder:
         L = self.length
         if L >= self.cap:
             raise ValueError("KV cache capacity exceeded")
-        dst = [buf[:, :, L:L + 1] for buf in self.qs + self.vs]
-        torch._foreach_copy_(dst, list(qs_new) + list(vs_new))     # one multi-tensor launch
+        bufs, srcs = self.qs + self.vs, list(qs_new) + list(vs_new)
+        if len(bufs) <= _lib.MAX_ROW_COPIES and all(x.is_cuda and x.dtype == self.dtype for x in srcs):
+            esz = bufs[0].element_size()
+            cps = self._copies
+            for c, buf, x in zip(cps, bufs, srcs):
+                c.src = x.data_ptr()
+                c.src_stride[0], c.src_stride[1] = x.stride(0) * esz, x.stride(1) * esz
+                c.dst = buf.data_ptr() + L * buf.stride(2) * esz
+            stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+            if lib.poly_copy_rows(cps, len(bufs), stream) == _lib.POLY_OK:   # one launch for every cache
+                return
+        dst = [buf[:, :, L:L + 1] for buf in bufs]
+        torch._foreach_copy_(dst, srcs)
 
     def step(self, q1_new, out=None):
         """Run the chain for the row appended last; returns out [b, h, 1, d]."""

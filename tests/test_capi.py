@@ -50,6 +50,14 @@ def test_invalid_args_report_errors_without_gpu():
     assert "divisible" in _lib.lib.poly_last_error().decode()
     a.heads, a.head_dim = 2, 512
     assert _lib.lib.poly_pass_fwd(ctypes.byref(a), None) == _lib.POLY_EUNSUPPORTED
+    # poly_copy_rows validates every copy before launching
+    rc = _lib.PolyRowCopy()
+    assert _lib.lib.poly_copy_rows(None, 1, None) == _lib.POLY_EINVAL
+    assert _lib.lib.poly_copy_rows(ctypes.byref(rc), 17, None) == _lib.POLY_EINVAL
+    assert _lib.lib.poly_copy_rows(ctypes.byref(rc), 0, None) == _lib.POLY_OK
+    rc.outer, rc.inner, rc.row_bytes, rc.src, rc.dst = 2, 2, 24, 16, 32
+    assert _lib.lib.poly_copy_rows(ctypes.byref(rc), 1, None) == _lib.POLY_EINVAL
+    assert "16-byte" in _lib.lib.poly_last_error().decode()
     # poly_decode_chain validates every pass before launching any
     assert _lib.lib.poly_decode_chain(None, 1, None) == _lib.POLY_EINVAL
     assert _lib.lib.poly_decode_chain(ctypes.byref(a), -1, None) == _lib.POLY_EINVAL

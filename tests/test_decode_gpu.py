@@ -161,3 +161,35 @@ def test_decode_chain_equals_level_by_level(order, d, h, g, L0):
     assert decs[0]._chain is True
     for m0, m1 in zip(decs[0].msgs + decs[0].lses, decs[1].msgs + decs[1].lses):
         assert torch.equal(m0[:, :, :L0 + steps], m1[:, :, :L0 + steps])
+
+
+def test_copy_rows_matches_slice_assignment():
+    """poly_copy_rows (every cache append of a step in one launch) writes the
+    same bytes as slice assignment, for strided sources and destinations of
+    several row sizes, and leaves every other row untouched."""
+    import ctypes
+    from poly_attention_b200 import _lib
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    dsts, srcs, refs = [], [], []
+    cps = (_lib.PolyRowCopy * 5)()
+    for i, (b, g, d, dt) in enumerate([(3, 4, 64, torch.bfloat16), (2, 1, 128, torch.float16), (5, 2, 8, torch.float32),
+                                       (1, 8, 128, torch.bfloat16), (4, 3, 96, torch.bfloat16)]):
+        cache = torch.randn(b, g, 50, d, device="cuda", generator=gen).to(dt)
+        src = torch.randn(b, 2 * g, 1, d, device="cuda", generator=gen).to(dt)[:, ::2]   # strided heads
+        row = 7 * i + 3
+        ref = cache.clone()
+        ref[:, :, row:row + 1] = src
+        e = cache.element_size()
+        c = cps[i]
+        c.src, c.dst = src.data_ptr(), cache.data_ptr() + row * cache.stride(2) * e
+        c.outer, c.inner, c.row_bytes = b, g, d * e
+        c.src_stride[0], c.src_stride[1] = src.stride(0) * e, src.stride(1) * e
+        c.dst_stride[0], c.dst_stride[1] = cache.stride(0) * e, cache.stride(1) * e
+        dsts.append(cache)
+        refs.append(ref)
+        srcs.append(src)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert _lib.lib.poly_copy_rows(cps, 5, stream) == _lib.POLY_OK
+    torch.cuda.synchronize()
+    for got, ref in zip(dsts, refs):
+        assert torch.equal(got, ref)
