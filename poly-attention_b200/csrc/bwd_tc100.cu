@@ -8,13 +8,15 @@
 // Per query tile t:
 //   S^T  = K Q_t^T        (M=128 keys, N=128 queries, K=64)   -> TMEM
 //   dP^T = V dO_t^T                                          -> TMEM
-//   softmax warpgroup (thread = key row j):
+//   two softmax warpgroups (thread = key row j, warpgroup hw takes query
+//   columns [64 hw, 64 hw + 64)):
 //     p = exp2(s*log2e*scale + bias_j - lse2_i), ds = p (dp - delta_i),
 //     dbias_j += ds (a register: the column sum of dS needs no reduction),
-//     P^T and dS^T (x softclamp factor) -> 128B-swizzled smem
-//   dV += P^T dO_t, dK += dS^T Q_t                         (TMEM accumulators)
-//   dQ_t = dS K  (A = the same dS^T tile read MN-major)    -> TMEM, double buffer
-//   dQ warpgroup: TMEM -> fp32 red.global.add into the dq accumulator
+//     P^T -> TMEM (16-bit), dS^T (x softclamp factor) -> 128B-swizzled smem
+//   dV += P^T dO_t (TS MMA, A from TMEM), dK += dS^T Q_t  (TMEM accumulators)
+//   dQ_t = dS K  (A = the same dS^T tile read MN-major)    -> TMEM
+//   dQ_t staging by warpgroup 0 once it has handed tile t + 1 to the MMA:
+//   TMEM -> swizzled fp32 smem -> TMA reduce-add into the fp32 accumulator
 // A preprocessing kernel forms delta_i = dout_i . out_i - dlse_i and the
 // log2-domain lse; a final kernel converts the fp32 dq accumulator.
 #include <mutex>
@@ -111,7 +113,7 @@ __device__ __forceinline__ void store_chunk(uint8_t* tile, int r, int c, const u
 // ds = p (dp - delta), d-bias += ds, dS = ds * softclamp'(s). MASK adds the
 // causal diagonal (queries il < diag_row) and invalid-key masks; the
 // unmasked variant is the common case and carries no per-element selects.
-template <typename T, bool SOFTCLAMP, bool HAS_BIAS, bool MASK>
+template <typename T, bool SOFTCLAMP, bool HAS_BIAS, bool MASK, bool DB>
 __device__ __forceinline__ void softmax_bwd_chunk(const uint32_t (&sv)[32], const uint32_t (&dv)[32],
                                                   const float* nl, const float* dl, float b2, const BwdParams& p,
                                                   bool key_ok, int il0, int diag_row, float& dbias,
@@ -140,7 +142,7 @@ __device__ __forceinline__ void softmax_bwd_chunk(const uint32_t (&sv)[32], cons
       float pr = ex2(x);
       if (MASK && (!key_ok || il0 + u < diag_row)) pr = 0.f;
       const float ds = pr * (__uint_as_float(dv[u]) - dd4[e]);
-      dbias += ds;
+      if (DB) dbias += ds;   // only when the caller wants the key-bias gradient
       pp[e] = pr;
       dd[e] = SOFTCLAMP ? ds * dfac : ds;
     }
@@ -151,7 +153,7 @@ __device__ __forceinline__ void softmax_bwd_chunk(const uint32_t (&sv)[32], cons
   }
 }
 
-template <typename T, bool SOFTCLAMP, bool HAS_BIAS>
+template <typename T, bool SOFTCLAMP, bool HAS_BIAS, bool DB>
 __global__ void __launch_bounds__(kThreads, 1)
     pass_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -391,10 +393,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* nl = sLse + s * BQ + c * 32;       // -lse2 of the chunk's queries
         const float* dl = sDel + s * BQ + c * 32;
         if (diag || !key_ok_warp)
-          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, true>(sv, dv, nl, dl, b2, p, key_ok, c * 32, diag ? r : -1,
+          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, true, DB>(sv, dv, nl, dl, b2, p, key_ok, c * 32, diag ? r : -1,
                                                           dbias, pw, dw);
         else
-          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, false>(sv, dv, nl, dl, b2, p, key_ok, c * 32, -1, dbias, pw,
+          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, false, DB>(sv, dv, nl, dl, b2, p, key_ok, c * 32, -1, dbias, pw,
                                                            dw);
         // P^T / dS^T smem is free once the previous tile's MMAs completed
         if (cc == 0 && t > 0 && !mbar_wait_warp(mma_done, (t - 1) & 1, abort_flag, err, 8)) {
@@ -561,13 +563,13 @@ BwdWs bwd_ws(const PolyPassBwdArgs& a) {
   return w;
 }
 
-template <typename T, bool SOFTCLAMP, bool HAS_BIAS>
+template <typename T, bool SOFTCLAMP, bool HAS_BIAS, bool DB>
 int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   using L = BwdLayout;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS>,
+    attr_err = cudaFuncSetAttribute(pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS, DB>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   });
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "cudaFuncSetAttribute(bwd tc)");
@@ -613,7 +615,7 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   p.dbias_stride[1] = a.dbias_stride[1];
   p.k_tiles = (f.seq_k + BK - 1) / BK;
   dim3 grid(p.k_tiles * f.batch * f.kv_heads);
-  pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
+  pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS, DB><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
   const int64_t cthreads = (int64_t)f.batch * f.heads * f.seq_q * (D / 8);
   bwd_dq_convert_kernel<T><<<(unsigned)((cthreads + 255) / 256), 256, 0, s>>>(a, w.dq_acc);
   note_launch(3);
@@ -622,9 +624,13 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
 
 template <typename T>
 int bwd_dispatch(const PolyPassBwdArgs& a, cudaStream_t s) {
-  const bool sc = a.fwd.softclamp > 0.f, bias = a.fwd.bias != nullptr;
-  if (sc) return bias ? launch_bwd_t<T, true, true>(a, s) : launch_bwd_t<T, true, false>(a, s);
-  return bias ? launch_bwd_t<T, false, true>(a, s) : launch_bwd_t<T, false, false>(a, s);
+  const bool sc = a.fwd.softclamp > 0.f, bias = a.fwd.bias != nullptr, db = a.dbias != nullptr;
+  if (db) {
+    if (sc) return bias ? launch_bwd_t<T, true, true, true>(a, s) : launch_bwd_t<T, true, false, true>(a, s);
+    return bias ? launch_bwd_t<T, false, true, true>(a, s) : launch_bwd_t<T, false, false, true>(a, s);
+  }
+  if (sc) return bias ? launch_bwd_t<T, true, true, false>(a, s) : launch_bwd_t<T, true, false, false>(a, s);
+  return bias ? launch_bwd_t<T, false, true, false>(a, s) : launch_bwd_t<T, false, false, false>(a, s);
 }
 
 }  // namespace
