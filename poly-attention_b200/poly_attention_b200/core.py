@@ -17,6 +17,8 @@ q1 at full head count. The reference repeats those tensors r times instead
 """
 from __future__ import annotations
 
+from typing import Optional, Tuple
+
 import torch
 
 from .ops import pass_bwd, pass_fwd
@@ -26,36 +28,91 @@ def _exists(v):
     return v is not None
 
 
-class _Order2(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, softclamp, causal):
-        shared = q2_pass1 is None
-        qp1 = q2 if shared else q2_pass1
-        # pass 1: q2 attends q3 (poly_attention/poly_attention.py:63-82)
-        msg, lse23 = pass_fwd(qp1, q3, v3, causal=causal, softclamp=softclamp, key_mask=cm2)
-        # pass 2: q1 attends q2 with lse23 as key bias (:91-114)
-        out, lse12 = pass_fwd(q1, q2, msg, causal=causal, softclamp=softclamp, bias=lse23, key_mask=cm1,
-                              query_mask=mask)
-        ctx.save_for_backward(q1, q2, q3, v3, qp1, msg, lse23, out, lse12, mask, cm1, cm2)
-        ctx.shared, ctx.softclamp, ctx.causal = shared, softclamp, causal
-        ctx.mark_non_differentiable(lse23, msg)
-        return out, lse23, msg
+# The order-2 core is two torch.library custom ops (forward, backward) with a
+# fake (shape) implementation and registered autograd, so torch.compile treats
+# it as one opaque node (no graph break at the ctypes calls) and autocast
+# regions work (inputs are cast to the autocast dtype first, as the
+# reference's einsums are).
 
-    @staticmethod
-    def backward(ctx, dout, _dlse, _dmsg):
-        q1, q2, q3, v3, qp1, msg, lse23, out, lse12, mask, cm1, cm2 = ctx.saved_tensors
-        sc, causal = ctx.softclamp, ctx.causal
-        # pass-2 backward: dq1, dq2 (as keys), dmsg (as values), dlse23 (key-bias grad)
-        dq1, dq2_keys, dmsg, dlse23 = pass_bwd(q1, q2, msg, out, lse12, dout, causal=causal, softclamp=sc,
-                                               bias=lse23, key_mask=cm1, query_mask=mask, want_dbias=True)
-        # pass-1 backward with the log-sum-exp gradient folded in; dq2 parts summed in-kernel
-        if ctx.shared:
-            dq2, dq3, dv3, _ = pass_bwd(qp1, q3, v3, msg, lse23, dmsg, causal=causal, softclamp=sc, key_mask=cm2,
-                                        dlse=dlse23, dq=dq2_keys, dq_accumulate=True)
-            return dq1, dq2, dq3, dv3, None, None, None, None, None, None
-        dqp1, dq3, dv3, _ = pass_bwd(qp1, q3, v3, msg, lse23, dmsg, causal=causal, softclamp=sc, key_mask=cm2,
-                                     dlse=dlse23)
-        return dq1, dq2_keys, dq3, dv3, dqp1, None, None, None, None, None
+def _sc(softclamp):
+    return float(softclamp) if softclamp else 0.0
+
+
+@torch.library.custom_op("poly_b200::order2_fwd", mutates_args=())
+def _order2_fwd(q1: torch.Tensor, q2: torch.Tensor, q3: torch.Tensor, v3: torch.Tensor,
+                q2_pass1: Optional[torch.Tensor], mask: Optional[torch.Tensor], cm1: Optional[torch.Tensor],
+                cm2: Optional[torch.Tensor], softclamp: float, causal: bool
+                ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Both passes: returns (out, lse23, msg, lse12)."""
+    sc = softclamp or None
+    qp1 = q2 if q2_pass1 is None else q2_pass1
+    # pass 1: q2 attends q3 (poly_attention/poly_attention.py:63-82)
+    msg, lse23 = pass_fwd(qp1, q3, v3, causal=causal, softclamp=sc, key_mask=cm2)
+    # pass 2: q1 attends q2 with lse23 as key bias (:91-114)
+    out, lse12 = pass_fwd(q1, q2, msg, causal=causal, softclamp=sc, bias=lse23, key_mask=cm1, query_mask=mask)
+    return out, lse23, msg, lse12
+
+
+@_order2_fwd.register_fake
+def _(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, softclamp, causal):
+    qp1 = q2 if q2_pass1 is None else q2_pass1
+    f32 = torch.float32
+    return (q1.new_empty(q1.shape), qp1.new_empty(qp1.shape[:3], dtype=f32),
+            qp1.new_empty((*qp1.shape[:3], v3.shape[-1])), q1.new_empty(q1.shape[:3], dtype=f32))
+
+
+@torch.library.custom_op("poly_b200::order2_bwd", mutates_args=())
+def _order2_bwd(q1: torch.Tensor, q2: torch.Tensor, q3: torch.Tensor, v3: torch.Tensor,
+                q2_pass1: Optional[torch.Tensor], mask: Optional[torch.Tensor], cm1: Optional[torch.Tensor],
+                cm2: Optional[torch.Tensor], msg: torch.Tensor, lse23: torch.Tensor, out: torch.Tensor,
+                lse12: torch.Tensor, dout: torch.Tensor, softclamp: float, causal: bool
+                ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (dq1, dq2, dq3, dv3, dq2_pass1); dq2_pass1 is empty when q2_pass1 is None."""
+    sc = softclamp or None
+    # pass-2 backward: dq1, dq2 (as keys), dmsg (as values), dlse23 (key-bias grad)
+    dq1, dq2_keys, dmsg, dlse23 = pass_bwd(q1, q2, msg, out, lse12, dout, causal=causal, softclamp=sc,
+                                           bias=lse23, key_mask=cm1, query_mask=mask, want_dbias=True)
+    # pass-1 backward with the log-sum-exp gradient folded in; dq2 parts summed in-kernel
+    if q2_pass1 is None:
+        dq2, dq3, dv3, _ = pass_bwd(q2, q3, v3, msg, lse23, dmsg, causal=causal, softclamp=sc, key_mask=cm2,
+                                    dlse=dlse23, dq=dq2_keys, dq_accumulate=True)
+        return dq1, dq2, dq3, dv3, q2.new_empty(0)
+    dqp1, dq3, dv3, _ = pass_bwd(q2_pass1, q3, v3, msg, lse23, dmsg, causal=causal, softclamp=sc, key_mask=cm2,
+                                 dlse=dlse23)
+    return dq1, dq2_keys, dq3, dv3, dqp1
+
+
+@_order2_bwd.register_fake
+def _(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, msg, lse23, out, lse12, dout, softclamp, causal):
+    dqp1 = q2.new_empty(0) if q2_pass1 is None else q2_pass1.new_empty(q2_pass1.shape)
+    return (q1.new_empty(q1.shape), q2.new_empty(q2.shape), q3.new_empty(q3.shape), v3.new_empty(v3.shape), dqp1)
+
+
+def _order2_setup(ctx, inputs, output):
+    q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, softclamp, causal = inputs
+    out, lse23, msg, lse12 = output
+    ctx.save_for_backward(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, msg, lse23, out, lse12)
+    ctx.softclamp, ctx.causal = softclamp, causal
+    ctx.mark_non_differentiable(lse23, msg, lse12)
+
+
+def _order2_backward(ctx, dout, _dlse23, _dmsg, _dlse12):
+    q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, msg, lse23, out, lse12 = ctx.saved_tensors
+    dq1, dq2, dq3, dv3, dqp1 = _order2_bwd(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, msg, lse23, out, lse12,
+                                           dout.contiguous(), ctx.softclamp, ctx.causal)
+    return dq1, dq2, dq3, dv3, (dqp1 if q2_pass1 is not None else None), None, None, None, None, None
+
+
+_order2_fwd.register_autograd(_order2_backward, setup_context=_order2_setup)
+
+
+def _autocast(*ts):
+    """Inside a CUDA autocast region, cast the floating inputs of the attention
+    core to the autocast dtype (the reference's einsums run in it there)."""
+    if not torch.is_autocast_enabled("cuda"):
+        return ts
+    dt = torch.get_autocast_dtype("cuda")
+    return tuple(t.to(dt) if t is not None and t.is_floating_point() and t.dtype != dt else t for t in ts)
 
 
 def poly_attention_order2(q1, q2, q3, v3, *, q2_pass1=None, mask=None, context_mask=None, softclamp_value=None,
@@ -68,7 +125,9 @@ def poly_attention_order2(q1, q2, q3, v3, *, q2_pass1=None, mask=None, context_m
     reference_poly_attention. lse23 / msg are at g heads.
     """
     cm1, cm2 = context_mask if _exists(context_mask) else (None, None)
-    return _Order2.apply(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, softclamp_value, bool(causal))
+    q1, q2, q3, v3, q2_pass1 = _autocast(q1, q2, q3, v3, q2_pass1)
+    out, lse23, msg, _ = _order2_fwd(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, _sc(softclamp_value), bool(causal))
+    return out, lse23, msg
 
 
 def poly_attention_order2_cached(q1, q2_new, q2_full, q3_full, v3_full, lse_cache, msg_cache, *,
@@ -163,6 +222,7 @@ def poly_attention_chain(q_left, q_right, vs, *, softclamp_value=None, causal=Fa
     """
     order = len(q_left)
     cms = tuple(context_masks) if context_masks is not None else (None,) * order
+    q_left, q_right, vs = list(_autocast(*q_left)), list(_autocast(*q_right)), list(_autocast(*vs))
     res = _Chain.apply(order, softclamp_value, bool(causal), mask, cms, *q_left, *q_right, *vs)
     return res[0], res[1:order], res[order:]
 
