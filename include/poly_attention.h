@@ -196,6 +196,35 @@ typedef struct {
 POLY_API int poly_copy_rows(const PolyRowCopy* copies, int n, void* stream);
 
 /*
+ * Per-head RMSNorm of query/key tensors straight from the head-split view of a
+ * projection output (replaces q_norms, poly_attention/poly_attention.py:272,
+ * n_poly_attention.py:186-187, and the contiguous copy torch makes of the
+ * strided view first): dst = src * rsqrt(mean(src^2) + eps) * weight over the
+ * last dim, fp32 arithmetic. src [batch, heads, rows, dim] with element
+ * strides (batch, head, row), last dim contiguous; dst contiguous, in
+ * dst_dtype (src's dtype, or F32 inside autocast). weight [dim] in
+ * weight_dtype. dim <= 256, dim % 8 == 0, 16-byte aligned rows. All n <= 4
+ * tensors are normalised in ONE kernel launch.
+ */
+#define POLY_MAX_NORMS 4
+typedef struct {
+  const void* src;
+  void* dst;
+  const void* weight;
+  int32_t batch;
+  int32_t heads;
+  int32_t rows;
+  int32_t dim;
+  int64_t src_stride[3]; /* elements: batch, head, row */
+  int32_t src_dtype;     /* POLY_F32 / POLY_F16 / POLY_BF16 */
+  int32_t dst_dtype;
+  int32_t weight_dtype;
+  float eps;
+} PolyHeadNorm;
+
+POLY_API int poly_head_rmsnorm(const PolyHeadNorm* norms, int n, void* stream);
+
+/*
  * poly_pass_bwd without a caller workspace. No counterpart in the reference:
  * it exists for callers that cannot allocate device memory (FFI hosts that
  * only pass existing buffers, processes whose device memory another

@@ -114,6 +114,10 @@ int poly_pass_fwd(const PolyPassArgs* a, void* stream) {
   }
 }
 
+int poly_head_rmsnorm(const PolyHeadNorm* norms, int n, void* stream) {
+  return head_rmsnorm(norms, n, (cudaStream_t)stream);
+}
+
 int poly_copy_rows(const PolyRowCopy* copies, int n, void* stream) {
   return copy_rows(copies, n, (cudaStream_t)stream);
 }

@@ -77,5 +77,6 @@ bool pass_decode_eligible(const PolyPassArgs& a);
 int launch_pass_decode(const PolyPassArgs& a, cudaStream_t s, bool dependent = false);
 size_t pass_decode_workspace(const PolyPassArgs& a);
 int copy_rows(const PolyRowCopy* copies, int n, cudaStream_t s);
+int head_rmsnorm(const PolyHeadNorm* norms, int n, cudaStream_t s);
 
 }  // namespace poly

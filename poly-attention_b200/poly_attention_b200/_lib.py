@@ -68,6 +68,16 @@ class PolyRowCopy(ctypes.Structure):
 
 MAX_ROW_COPIES = 16
 
+
+class PolyHeadNorm(ctypes.Structure):
+    _fields_ = [("src", c_vp), ("dst", c_vp), ("weight", c_vp), ("batch", ctypes.c_int32),
+                ("heads", ctypes.c_int32), ("rows", ctypes.c_int32), ("dim", ctypes.c_int32),
+                ("src_stride", ctypes.c_int64 * 3), ("src_dtype", ctypes.c_int32), ("dst_dtype", ctypes.c_int32),
+                ("weight_dtype", ctypes.c_int32), ("eps", ctypes.c_float)]
+
+
+MAX_NORMS = 4
+
 EXPORTS = {
     "poly_pass_fwd": (ctypes.c_int, [ctypes.POINTER(PolyPassArgs), c_vp]),
     "poly_pass_fwd_workspace_size": (c_sz, [ctypes.POINTER(PolyPassArgs)]),
@@ -76,6 +86,7 @@ EXPORTS = {
     "poly_lse_merge": (ctypes.c_int, [ctypes.POINTER(PolyMergeArgs), c_vp]),
     "poly_decode_chain": (ctypes.c_int, [ctypes.POINTER(PolyPassArgs), ctypes.c_int, c_vp]),
     "poly_copy_rows": (ctypes.c_int, [ctypes.POINTER(PolyRowCopy), ctypes.c_int, c_vp]),
+    "poly_head_rmsnorm": (ctypes.c_int, [ctypes.POINTER(PolyHeadNorm), ctypes.c_int, c_vp]),
     "poly_pass_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(PolyPassBwdArgs), c_vp]),
     "poly_noalloc_scratch_bytes": (c_sz, []),
     "poly_pass_fwd_kernel_name": (ctypes.c_char_p, [ctypes.POINTER(PolyPassArgs)]),

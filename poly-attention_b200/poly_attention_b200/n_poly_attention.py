@@ -12,6 +12,7 @@ from torch import Tensor, nn
 from torch.nn import Module, RMSNorm
 
 from .core import poly_attention_chain, poly_attention_chain_cached
+from .head_norm import head_rmsnorm
 from .poly_attention import _rotary, cast_tuple, default, exists, merge_heads, split_heads
 
 LinearNoBias = partial(nn.Linear, bias=False)
@@ -101,7 +102,7 @@ class NPolyAttention(Module):
         else:
             vs = tuple(kv[1] for kv in kvs_rest)
             root_value = kv1[1] if self.has_root_v else None
-        qs = tuple(norm(q) for norm, q in zip(self.q_norms, (q1, *qs_rest)))
+        qs = tuple(head_rmsnorm(self.q_norms, (q1, *qs_rest)))
         if exists(rotary_pos_emb):
             r = _rotary()
             qs = tuple(r.apply_rotary_emb(rotary_pos_emb, q) for q in qs)

@@ -13,6 +13,7 @@ from torch import Tensor, nn
 from torch.nn import Module, RMSNorm
 
 from .core import poly_attention_order2, poly_attention_order2_cached
+from .head_norm import head_rmsnorm
 
 LinearNoBias = partial(nn.Linear, bias=False)
 
@@ -135,7 +136,7 @@ class Order2PolyAttention(Module):
             q2 = kv1[0]
             v2 = kv1[1] if self.has_root_v else None
             q3, v3 = kv2[0], kv2[1]
-        q1, q2, q3 = (norm(q) for norm, q in zip(self.q_norms, (q1, q2, q3)))
+        q1, q2, q3 = head_rmsnorm(self.q_norms, (q1, q2, q3))
         if exists(rotary_pos_emb):
             r = _rotary()
             q1, q2, q3 = (r.apply_rotary_emb(rotary_pos_emb, q) for q in (q1, q2, q3))
