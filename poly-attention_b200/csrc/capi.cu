@@ -39,11 +39,12 @@ static int check_pass(const PolyPassArgs* a) {
   return POLY_OK;
 }
 
-enum class FwdKind { kSimt, kTc, kDecode };
+enum class FwdKind { kSimt, kTc, kDecode, kSmall };
 
 static FwdKind choose_fwd(const PolyPassArgs& a) {
   if (force_simt()) return FwdKind::kSimt;
   if (pass_decode_eligible(a)) return FwdKind::kDecode;
+  if (pass_small_eligible(a)) return FwdKind::kSmall;
   if (pass_fwd_tc_eligible(a)) return FwdKind::kTc;
   return FwdKind::kSimt;
 }
@@ -91,6 +92,7 @@ const char* poly_pass_fwd_kernel_name(const PolyPassArgs* a) {
   if (check_pass(a) != POLY_OK) return "invalid";
   switch (choose_fwd(*a)) {
     case FwdKind::kDecode: return "decode";
+    case FwdKind::kSmall: return "small";
     case FwdKind::kTc: return "tc100";
     default: return "simt";
   }
@@ -109,6 +111,7 @@ int poly_pass_fwd(const PolyPassArgs* a, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   switch (kind) {
     case FwdKind::kDecode: return launch_pass_decode(*a, s);
+    case FwdKind::kSmall: return launch_pass_small(*a, s);
     case FwdKind::kTc: return launch_pass_fwd_tc(*a, s);
     default: return launch_pass_fwd_simt(*a, s);
   }
