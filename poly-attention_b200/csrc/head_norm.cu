@@ -29,57 +29,91 @@ __device__ __forceinline__ T st_f(float x) { return from_f32<T>(x); }
 template <>
 __device__ __forceinline__ float st_f<float>(float x) { return x; }
 
-template <typename TS, typename TD, typename TW>
+template <typename TS, typename TD, typename TW, int NJ>
 __global__ void __launch_bounds__(256) head_rmsnorm_kernel(const Norms P) {
-  constexpr int VEC = 16 / sizeof(TS);   // elements per 16-byte chunk
+  constexpr int VEC = 16 / sizeof(TS);   // elements per 16-byte chunk; a lane owns NJ chunks of a row
+  constexpr int NR = 2;                  // rows per lane group per iteration (loads in flight)
   const int lane = threadIdx.x & 31, sub = lane >> 3, li = lane & 7;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t total = P.start[P.n];
-  for (int64_t r0 = warp * 4; r0 < total; r0 += nwarps * 4) {
-    const int64_t r = r0 + sub;
-    const bool ok = r < total;
-    int k = 0;
-    while (k + 1 < P.n && r >= P.start[k + 1]) ++k;
-    const PolyHeadNorm& d = P.d[k];
-    const int64_t local = ok ? r - P.start[k] : 0;
-    const int64_t ni = local % d.rows, t = local / d.rows;
-    const int64_t hi = t % d.heads, bi = t / d.heads;
-    const TS* src = (const TS*)d.src + bi * d.src_stride[0] + hi * d.src_stride[1] + ni * d.src_stride[2];
-    const int chunks = d.dim / VEC;   // 16-byte chunks per row; lane li takes li, li + 8, ...
-    float v[32];
-    float ss = 0.f;
+  for (int64_t r0 = warp * 4 * NR; r0 < total; r0 += nwarps * 4 * NR) {
+    float v[NR][NJ * VEC];
+    float ss[NR];
+    const TS* src[NR];
+    int kd[NR];
+    int64_t dst_row[NR];
 #pragma unroll
-    for (int j = 0; j < 32 / VEC; ++j) {
-      const int c = li + 8 * j;
-      if (ok && c < chunks) {
-        const uint4 u = *reinterpret_cast<const uint4*>(src + c * VEC);
-        const TS* e = reinterpret_cast<const TS*>(&u);
+    for (int u = 0; u < NR; ++u) {
+      const int64_t r = r0 + u * 4 + sub;
+      const bool ok = r < total;
+      int k = 0;
+      while (k + 1 < P.n && r >= P.start[k + 1]) ++k;
+      const PolyHeadNorm& d = P.d[k];
+      const int64_t local = ok ? r - P.start[k] : 0;
+      const int64_t ni = local % d.rows, t = local / d.rows;
+      const int64_t hi = t % d.heads, bi = t / d.heads;
+      kd[u] = ok ? k : -1;
+      src[u] = (const TS*)d.src + bi * d.src_stride[0] + hi * d.src_stride[1] + ni * d.src_stride[2];
+      dst_row[u] = ((bi * d.heads + hi) * d.rows + ni) * d.dim;
+    }
 #pragma unroll
-        for (int q = 0; q < VEC; ++q) {
-          v[j * VEC + q] = ld_f<TS>(e, q);
-          ss = fmaf(v[j * VEC + q], v[j * VEC + q], ss);
+    for (int u = 0; u < NR; ++u) {
+      const int chunks = kd[u] >= 0 ? P.d[kd[u]].dim / VEC : 0;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int c = li + 8 * j;
+        if (c < chunks) {
+          const uint4 q4 = *reinterpret_cast<const uint4*>(src[u] + c * VEC);
+          const TS* e = reinterpret_cast<const TS*>(&q4);
+#pragma unroll
+          for (int q = 0; q < VEC; ++q) v[u][j * VEC + q] = ld_f<TS>(e, q);
+        } else {
+#pragma unroll
+          for (int q = 0; q < VEC; ++q) v[u][j * VEC + q] = 0.f;
         }
-      } else {
-#pragma unroll
-        for (int q = 0; q < VEC; ++q) v[j * VEC + q] = 0.f;
       }
     }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-    if (!ok) continue;
-    const float rs = rsqrtf(ss / (float)d.dim + d.eps);
-    const TW* w = (const TW*)d.weight;
-    TD* dst = (TD*)d.dst + (((bi * d.heads + hi) * d.rows + ni) * d.dim);
 #pragma unroll
-    for (int j = 0; j < 32 / VEC; ++j) {
-      const int c = li + 8 * j;
-      if (c < chunks) {
+    for (int u = 0; u < NR; ++u) {
+      float a = 0.f;
 #pragma unroll
-        for (int q = 0; q < VEC; ++q) {
-          const int i = c * VEC + q;
-          dst[i] = st_f<TD>(v[j * VEC + q] * rs * ld_f<TW>(w, i));
+      for (int i = 0; i < NJ * VEC; ++i) a = fmaf(v[u][i], v[u][i], a);
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      a += __shfl_xor_sync(0xffffffffu, a, 2);
+      a += __shfl_xor_sync(0xffffffffu, a, 4);
+      ss[u] = a;
+    }
+#pragma unroll
+    for (int u = 0; u < NR; ++u) {
+      if (kd[u] < 0) continue;
+      const PolyHeadNorm& d = P.d[kd[u]];
+      const float rs = rsqrtf(ss[u] / (float)d.dim + d.eps);
+      const int chunks = d.dim / VEC;
+      const TW* w = (const TW*)d.weight;
+      TD* dst = (TD*)d.dst + dst_row[u];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int c = li + 8 * j;
+        if (c < chunks) {
+          // weights and outputs of the chunk as 16-byte vectors
+          float wv[VEC];
+#pragma unroll
+          for (int q0 = 0; q0 < VEC; q0 += 16 / (int)sizeof(TW)) {
+            const uint4 q4 = *reinterpret_cast<const uint4*>(w + c * VEC + q0);
+            const TW* e = reinterpret_cast<const TW*>(&q4);
+#pragma unroll
+            for (int q = 0; q < 16 / (int)sizeof(TW); ++q) wv[q0 + q] = ld_f<TW>(e, q);
+          }
+          constexpr int OV = 16 / sizeof(TD);   // outputs per 16-byte store
+#pragma unroll
+          for (int q0 = 0; q0 < VEC; q0 += OV) {
+            uint4 q4;
+            TD* e = reinterpret_cast<TD*>(&q4);
+#pragma unroll
+            for (int q = 0; q < OV; ++q) e[q] = st_f<TD>(v[u][j * VEC + q0 + q] * rs * wv[q0 + q]);
+            *reinterpret_cast<uint4*>(dst + c * VEC + q0) = q4;
+          }
         }
       }
     }
@@ -93,9 +127,16 @@ int bad(const std::string& m) {
 
 template <typename TS, typename TD, typename TW>
 int launch(const Norms& P, cudaStream_t s) {
-  const int64_t warps = (P.start[P.n] + 3) / 4;
+  const int64_t warps = (P.start[P.n] + 7) / 8;
   const int64_t blocks = (warps * 32 + 255) / 256;
-  head_rmsnorm_kernel<TS, TD, TW><<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(P);
+  const unsigned grid = (unsigned)(blocks < 148 * 16 ? blocks : 148 * 16);
+  constexpr int VEC = 16 / sizeof(TS);
+  int maxdim = 0;
+  for (int i = 0; i < P.n; ++i) maxdim = P.d[i].dim > maxdim ? P.d[i].dim : maxdim;
+  const int nj = (maxdim / VEC + 7) / 8;   // chunks per lane for the widest row
+  if (nj <= 1) head_rmsnorm_kernel<TS, TD, TW, 1><<<grid, 256, 0, s>>>(P);
+  else if (nj <= 2) head_rmsnorm_kernel<TS, TD, TW, 2><<<grid, 256, 0, s>>>(P);
+  else head_rmsnorm_kernel<TS, TD, TW, 32 / VEC><<<grid, 256, 0, s>>>(P);
   note_launch(1);
   return cuda_status(cudaGetLastError(), "head_rmsnorm launch");
 }
@@ -130,9 +171,10 @@ int head_rmsnorm(const PolyHeadNorm* norms, int n, cudaStream_t s) {
     const int esz = d.src_dtype == POLY_F32 ? 4 : 2;
     if (d.dim <= 0 || d.dim > 256 || d.dim % 8) return bad(at + "dim must be a multiple of 8 in [8, 256]");
     const int64_t cnt = (int64_t)d.batch * d.heads * d.rows;
-    if (cnt && (!d.src || !d.dst || !d.weight || ((uintptr_t)d.src & 15) ||
+    if (cnt && (!d.src || !d.dst || !d.weight || ((uintptr_t)d.src & 15) || ((uintptr_t)d.dst & 15) ||
+                ((uintptr_t)d.weight & 15) ||
                 ((d.src_stride[0] * esz) & 15) || ((d.src_stride[1] * esz) & 15) || ((d.src_stride[2] * esz) & 15)))
-      return bad(at + "needs 16-byte aligned rows (pointer and strides)");
+      return bad(at + "needs 16-byte aligned src rows (pointer and strides), dst and weight");
     P.d[i] = d;
     P.start[i + 1] = P.start[i] + cnt;
   }

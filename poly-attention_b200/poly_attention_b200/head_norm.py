@@ -82,7 +82,8 @@ def head_rmsnorm(norms, xs):
     """Apply ``norms[i]`` (nn.RMSNorm over the last dim) to ``xs[i]`` ([b, h, n, d]
     views); CUDA tensors of one dtype go through the library in one launch."""
     usable = (all(x.is_cuda and x.dim() == 4 and x.dtype in _DTYPES and x.stride(-1) == 1 for x in xs) and
-              all(nm.weight is not None and nm.weight.dtype in (x.dtype, torch.float32)
+              all(nm.weight is not None and nm.weight.dtype in (x.dtype, torch.float32) and
+                  nm.weight.is_contiguous() and nm.weight.data_ptr() % 16 == 0
                   for nm, x in zip(norms, xs)) and len({x.dtype for x in xs}) == 1 and
               len({nm.weight.dtype for nm in norms}) == 1 and
               all(x.shape[-1] % 8 == 0 and x.shape[-1] <= 256 for x in xs))

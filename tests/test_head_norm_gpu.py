@@ -48,12 +48,12 @@ def test_head_rmsnorm_autocast_and_fp32_weights():
         refs = [nm(x) for nm, x in zip(norms, xs)]
     for g, r in zip(got, refs):
         assert g.dtype == r.dtype
-        torch.testing.assert_close(g.float(), r.float(), atol=1e-2, rtol=1e-2)
+        torch.testing.assert_close(g.float(), r.float(), atol=2e-2, rtol=1e-2)
     got = head_rmsnorm(norms, xs)                         # outside autocast: bf16 x, fp32 weight
     for g, nm, x in zip(got, norms, xs):
         r = nm(x)
         assert g.dtype == r.dtype
-        torch.testing.assert_close(g.float(), r.float(), atol=1e-2, rtol=1e-2)
+        torch.testing.assert_close(g.float(), r.float(), atol=2e-2, rtol=1e-2)
 
 
 def test_head_rmsnorm_gradients():
