@@ -34,6 +34,21 @@ def _exists(v):
 # regions work (inputs are cast to the autocast dtype first, as the
 # reference's einsums are).
 
+def _token_major(q):
+    """Output buffer [b, h, n, d] laid out as [b, n, h, d] in memory, so that the
+    modules' merge_heads ('b h n d -> b n (h d)', poly_attention.py:340) is a
+    view instead of a copy."""
+    b, h, n, d = q.shape
+    return q.new_empty((b, n, h, d)).permute(0, 2, 1, 3)
+
+
+def _dense(t):
+    """t itself when every stride is positive (any layout the kernels read
+    through strides, e.g. the token-major gradient of merge_heads), else a
+    contiguous copy (broadcast gradients such as out.sum().backward())."""
+    return t if all(st > 0 for st in t.stride()) else t.contiguous()
+
+
 def _sc(softclamp):
     return float(softclamp) if softclamp else 0.0
 
@@ -48,8 +63,9 @@ def _order2_fwd(q1: torch.Tensor, q2: torch.Tensor, q3: torch.Tensor, v3: torch.
     qp1 = q2 if q2_pass1 is None else q2_pass1
     # pass 1: q2 attends q3 (poly_attention/poly_attention.py:63-82)
     msg, lse23 = pass_fwd(qp1, q3, v3, causal=causal, softclamp=sc, key_mask=cm2)
-    # pass 2: q1 attends q2 with lse23 as key bias (:91-114)
-    out, lse12 = pass_fwd(q1, q2, msg, causal=causal, softclamp=sc, bias=lse23, key_mask=cm1, query_mask=mask)
+    # pass 2: q1 attends q2 with lse23 as key bias (:91-114), written token-major
+    out, lse12 = pass_fwd(q1, q2, msg, causal=causal, softclamp=sc, bias=lse23, key_mask=cm1, query_mask=mask,
+                          out=_token_major(q1))
     return out, lse23, msg, lse12
 
 
@@ -57,7 +73,7 @@ def _order2_fwd(q1: torch.Tensor, q2: torch.Tensor, q3: torch.Tensor, v3: torch.
 def _(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, softclamp, causal):
     qp1 = q2 if q2_pass1 is None else q2_pass1
     f32 = torch.float32
-    return (q1.new_empty(q1.shape), qp1.new_empty(qp1.shape[:3], dtype=f32),
+    return (_token_major(q1), qp1.new_empty(qp1.shape[:3], dtype=f32),
             qp1.new_empty((*qp1.shape[:3], v3.shape[-1])), q1.new_empty(q1.shape[:3], dtype=f32))
 
 
@@ -99,7 +115,7 @@ def _order2_setup(ctx, inputs, output):
 def _order2_backward(ctx, dout, _dlse23, _dmsg, _dlse12):
     q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, msg, lse23, out, lse12 = ctx.saved_tensors
     dq1, dq2, dq3, dv3, dqp1 = _order2_bwd(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, msg, lse23, out, lse12,
-                                           dout.contiguous(), ctx.softclamp, ctx.causal)
+                                           _dense(dout), ctx.softclamp, ctx.causal)
     return dq1, dq2, dq3, dv3, (dqp1 if q2_pass1 is not None else None), None, None, None, None, None
 
 
@@ -170,7 +186,7 @@ class _Chain(torch.autograd.Function):
             val, bias = nxt, lse
         vals[0], biases[0] = val, bias
         out, lse0 = pass_fwd(ql[0], qr[0], val, causal=causal, softclamp=softclamp, bias=bias, key_mask=cms[0],
-                             query_mask=mask)
+                             query_mask=mask, out=_token_major(ql[0]))
         outs[0], lses[0] = out, lse0
         ctx.order, ctx.softclamp, ctx.causal = order, softclamp, causal
         ctx.cms, ctx.mask = cms, mask

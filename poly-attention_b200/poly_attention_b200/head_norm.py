@@ -33,8 +33,12 @@ def _head_rmsnorm(xs: List[torch.Tensor], ws: List[torch.Tensor], eps: List[floa
     for g0 in range(0, len(xs), _lib.MAX_NORMS):
         idx = list(range(g0, min(len(xs), g0 + _lib.MAX_NORMS)))
         arr = (PolyHeadNorm * len(idx))()
+        keep = []
         for a, i in zip(arr, idx):
             x, w, o = xs[i], ws[i], outs[i]
+            if not w.is_contiguous() or w.data_ptr() % 16:      # the kernel reads weights as 16-byte vectors
+                w = w.contiguous().clone()
+                keep.append(w)
             b, h, n, d = x.shape
             a.src, a.dst, a.weight = x.data_ptr(), o.data_ptr(), w.data_ptr()
             a.batch, a.heads, a.rows, a.dim = b, h, n, d
@@ -82,8 +86,7 @@ def head_rmsnorm(norms, xs):
     """Apply ``norms[i]`` (nn.RMSNorm over the last dim) to ``xs[i]`` ([b, h, n, d]
     views); CUDA tensors of one dtype go through the library in one launch."""
     usable = (all(x.is_cuda and x.dim() == 4 and x.dtype in _DTYPES and x.stride(-1) == 1 for x in xs) and
-              all(nm.weight is not None and nm.weight.dtype in (x.dtype, torch.float32) and
-                  nm.weight.is_contiguous() and nm.weight.data_ptr() % 16 == 0
+              all(nm.weight is not None and nm.weight.dtype in (x.dtype, torch.float32)
                   for nm, x in zip(norms, xs)) and len({x.dtype for x in xs}) == 1 and
               len({nm.weight.dtype for nm in norms}) == 1 and
               all(x.shape[-1] % 8 == 0 and x.shape[-1] <= 256 for x in xs))
