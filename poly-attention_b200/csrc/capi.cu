@@ -39,12 +39,13 @@ static int check_pass(const PolyPassArgs* a) {
   return POLY_OK;
 }
 
-enum class FwdKind { kSimt, kTc, kDecode, kSmall };
+enum class FwdKind { kSimt, kTc, kDecode, kSmall, kF32 };
 
 static FwdKind choose_fwd(const PolyPassArgs& a) {
   if (force_simt()) return FwdKind::kSimt;
   if (pass_decode_eligible(a)) return FwdKind::kDecode;
   if (pass_small_eligible(a)) return FwdKind::kSmall;
+  if (pass_f32_eligible(a)) return FwdKind::kF32;
   if (pass_fwd_tc_eligible(a)) return FwdKind::kTc;
   return FwdKind::kSimt;
 }
@@ -93,6 +94,7 @@ const char* poly_pass_fwd_kernel_name(const PolyPassArgs* a) {
   switch (choose_fwd(*a)) {
     case FwdKind::kDecode: return "decode";
     case FwdKind::kSmall: return "small";
+    case FwdKind::kF32: return "tf32x3";
     case FwdKind::kTc: return "tc100";
     default: return "simt";
   }
@@ -112,6 +114,7 @@ int poly_pass_fwd(const PolyPassArgs* a, void* stream) {
   switch (kind) {
     case FwdKind::kDecode: return launch_pass_decode(*a, s);
     case FwdKind::kSmall: return launch_pass_small(*a, s);
+    case FwdKind::kF32: return launch_pass_f32(*a, s);
     case FwdKind::kTc: return launch_pass_fwd_tc(*a, s);
     default: return launch_pass_fwd_simt(*a, s);
   }

@@ -73,6 +73,8 @@ int read_device_error_dec(int* out, bool reset);
 bool pass_fwd_tc2_eligible(const PolyPassArgs& a);
 int launch_pass_fwd_tc2(const PolyPassArgs& a, cudaStream_t s);
 
+bool pass_f32_eligible(const PolyPassArgs& a);
+int launch_pass_f32(const PolyPassArgs& a, cudaStream_t s);
 bool pass_small_eligible(const PolyPassArgs& a);
 int launch_pass_small(const PolyPassArgs& a, cudaStream_t s);
 bool pass_decode_eligible(const PolyPassArgs& a);
