@@ -31,6 +31,8 @@
 // through HBM and no second kernel runs.
 #include <cooperative_groups.h>
 
+#include <cfloat>
+
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -386,13 +388,28 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
       L = fmaf(r[1], f, L);
     }
     const int h = g * R + rr;
+    float lse_v = (M + __log2f(L)) * kLn2;
+    if (M == -INFINITY) {
+      // every key dead: the reference's -finfo.max arithmetic gives the
+      // uniform average of the values (decode has no masks), lse = -FLT_MAX
+      const T* vg = (const T*)a.v + b * a.v_stride[0] + g * a.v_stride[1];
+      const T* mg = HAS_VMUL ? (const T*)a.v_mul + b * a.v_mul_stride[0] + g * a.v_mul_stride[1] : nullptr;
+      acc = 0.f;
+      for (int j = 0; j < a.seq_k; ++j) {
+        float vv = to_f32(vg[(int64_t)j * a.v_stride[2] + c]);
+        if (HAS_VMUL) vv = to_f32(from_f32<T>(vv * to_f32(mg[(int64_t)j * a.v_mul_stride[2] + c])));
+        acc += vv;
+      }
+      L = (float)a.seq_k;
+      lse_v = -FLT_MAX;
+    }
     const T ov = from_f32<T>(L > 0.f ? acc / L : 0.f);
     ((T*)a.out)[b * a.out_stride[0] + h * a.out_stride[1] + c] = ov;
     if (a.epi_out) {
       const T em = ((const T*)a.epi_mul)[b * a.epi_mul_stride[0] + h * a.epi_mul_stride[1] + c];
       ((T*)a.epi_out)[b * a.epi_out_stride[0] + h * a.epi_out_stride[1] + c] = from_f32<T>(to_f32(em) * to_f32(ov));
     }
-    if (a.lse && c == 0) a.lse[b * a.lse_stride[0] + h * a.lse_stride[1]] = (M + __log2f(L)) * kLn2;
+    if (a.lse && c == 0) a.lse[b * a.lse_stride[0] + h * a.lse_stride[1]] = lse_v;
   }
   cluster.sync();   // no CTA leaves while its record may still be read
 }

@@ -9,6 +9,7 @@
 // pass kernels: scale, softclamp, causal (top-left aligned), per-key bias in
 // the log2 domain with dead keys (bias <= -FLT_MAX / 2) dropped, lse in
 // natural-log units.
+#include <cfloat>
 #include <mutex>
 #include <type_traits>
 
@@ -186,18 +187,44 @@ __global__ void __launch_bounds__(256) pass_small_kernel(const PolyPassArgs a) {
       }
     }
   }
-  const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  bool fb0 = false, fb1 = false;   // row took the fully-excluded result
+  // A row whose every key is excluded (only dead keys can do that here) gets
+  // the reference's -finfo.max result: the uniform average over the keys that
+  // are not both causally masked and dead, lse = -FLT_MAX.
+  if (HAS_BIAS && (m0 == -INFINITY || m1 == -INFINITY)) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int row = hf ? r1 : r0;
+      if ((hf ? m1 : m0) != -INFINITY) continue;
+      int count = 0;
+#pragma unroll
+      for (int n = 0; n < NB; ++n) o[n][2 * hf] = o[n][2 * hf + 1] = 0.f;
+      for (int j = 0; j < nk; ++j) {
+        if (a.causal && j > row && sB[j] == -INFINITY) continue;
+        ++count;
+#pragma unroll
+        for (int n = 0; n < NB; ++n) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(sm + kMaxN * D * 2 + soff<D>(j, n) + 4 * tq);
+          const T* e = reinterpret_cast<const T*>(&w);
+          o[n][2 * hf] += to_f32(e[0]);
+          o[n][2 * hf + 1] += to_f32(e[1]);
+        }
+      }
+      if (hf) { l1 = (float)count; fb1 = true; } else { l0 = (float)count; fb0 = true; }
+    }
+  }
+  const float j0 = l0 > 0.f ? 1.f / l0 : 0.f, j1 = l1 > 0.f ? 1.f / l1 : 0.f;
   T* ob = (T*)a.out + b * a.out_stride[0] + h * a.out_stride[1];
 #pragma unroll
   for (int n = 0; n < NB; ++n) {
     const int c = n * 8 + 2 * tq;
-    if (r0 < nq) *reinterpret_cast<uint32_t*>(ob + (int64_t)r0 * a.out_stride[2] + c) = pk2<T>(o[n][0] * i0, o[n][1] * i0);
-    if (r1 < nq) *reinterpret_cast<uint32_t*>(ob + (int64_t)r1 * a.out_stride[2] + c) = pk2<T>(o[n][2] * i1, o[n][3] * i1);
+    if (r0 < nq) *reinterpret_cast<uint32_t*>(ob + (int64_t)r0 * a.out_stride[2] + c) = pk2<T>(o[n][0] * j0, o[n][1] * j0);
+    if (r1 < nq) *reinterpret_cast<uint32_t*>(ob + (int64_t)r1 * a.out_stride[2] + c) = pk2<T>(o[n][2] * j1, o[n][3] * j1);
   }
   if (a.lse && tq == 0) {
     float* lb = a.lse + b * a.lse_stride[0] + h * a.lse_stride[1];
-    if (r0 < nq) lb[r0] = (m0 + __log2f(l0)) * kLn2;
-    if (r1 < nq) lb[r1] = (m1 + __log2f(l1)) * kLn2;
+    if (r0 < nq) lb[r0] = fb0 ? -FLT_MAX : (m0 + __log2f(l0)) * kLn2;
+    if (r1 < nq) lb[r1] = fb1 ? -FLT_MAX : (m1 + __log2f(l1)) * kLn2;
   }
 }
 

@@ -193,3 +193,28 @@ def test_copy_rows_matches_slice_assignment():
     torch.cuda.synchronize()
     for got, ref in zip(dsts, refs):
         assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("vmul", [False, True])
+def test_decode_fully_dead_keys(vmul):
+    """Every cached key dead for one sequence (its previous-level rows were
+    fully masked): the reference's uniform average of the values, lse = -FLT_MAX."""
+    import poly_attention_b200 as P
+    dt = torch.bfloat16
+    b, h, g, L, d = 2, 8, 2, 300, 128
+    q = host(dev(rnd((b, h, 1, d), 21), dt))
+    k, v, vm = (host(dev(rnd((b, g, L, d), s), dt)) for s in (22, 23, 24))
+    bias = rnd((b, g, L), 25)
+    bias[0] = -np.finfo(np.float32).max
+    kw = {"bias": dev(bias, torch.float32)}
+    vv = v
+    if vmul:
+        kw["v_mul"] = dev(vm, dt)
+        vv = host(dev(v * vm, dt))
+    qt, kt, vt = dev(q, dt), dev(k, dt), dev(v, dt)
+    assert P.kernel_names(qt, kt, vt)[0] == "decode"
+    out, lse = P.pass_fwd(qt, kt, vt, **kw)
+    r = h // g
+    eo_, el = O.pass_fwd(q, np.repeat(k, r, 1), np.repeat(vv, r, 1), bias=np.repeat(bias, r, 1))
+    np.testing.assert_allclose(host(out), eo_, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(host(lse), el, atol=ATOL, rtol=RTOL)

@@ -63,3 +63,19 @@ def test_small_pass_strided_inputs():
     eo, el = O.pass_fwd(qf, kf, vf)
     np.testing.assert_allclose(host(out), eo, atol=ATOL, rtol=RTOL)
     np.testing.assert_allclose(host(lse), el, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_small_pass_fully_dead_rows(causal):
+    """Every key dead for one sequence: the reference's uniform-average result
+    (keys both causally masked and dead drop out), lse = -FLT_MAX."""
+    import poly_attention_b200 as P
+    dt = torch.bfloat16
+    b, h, n, d = 2, 2, 50, 64
+    q, k, v = (host(dev(rnd((b, h, n, d), s), dt)) for s in (5, 6, 7))
+    bias = rnd((b, h, n), 8)
+    bias[1] = -np.finfo(np.float32).max
+    out, lse = P.pass_fwd(dev(q, dt), dev(k, dt), dev(v, dt), causal=causal, bias=dev(bias, torch.float32))
+    eo, el = O.pass_fwd(q, k, v, causal=causal, bias=bias)
+    np.testing.assert_allclose(host(out), eo, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(host(lse), el, atol=ATOL, rtol=RTOL)
