@@ -49,6 +49,22 @@ def _dense(t):
     return t if all(st > 0 for st in t.stride()) else t.contiguous()
 
 
+def _propagate_masks(cms):
+    """Levels run from the last score to the first; once one level is masked,
+    its lse (the next level's key bias) can hold fully excluded rows
+    (-finfo.max), so every later level without a mask gets an all-true key
+    mask: that routes it to the masked-pass kernels, which reproduce the
+    reference's result for keys that are all dead."""
+    cms = list(cms)
+    seen = None
+    for t in range(len(cms) - 1, -1, -1):
+        if cms[t] is not None:
+            seen = cms[t]
+        elif seen is not None:
+            cms[t] = torch.ones_like(seen, dtype=torch.bool)
+    return tuple(cms)
+
+
 def _sc(softclamp):
     return float(softclamp) if softclamp else 0.0
 
@@ -141,6 +157,7 @@ def poly_attention_order2(q1, q2, q3, v3, *, q2_pass1=None, mask=None, context_m
     reference_poly_attention. lse23 / msg are at g heads.
     """
     cm1, cm2 = context_mask if _exists(context_mask) else (None, None)
+    cm1, cm2 = _propagate_masks((cm1, cm2))
     q1, q2, q3, v3, q2_pass1 = _autocast(q1, q2, q3, v3, q2_pass1)
     out, lse23, msg, _ = _order2_fwd(q1, q2, q3, v3, q2_pass1, mask, cm1, cm2, _sc(softclamp_value), bool(causal))
     return out, lse23, msg
@@ -153,7 +170,7 @@ def poly_attention_order2_cached(q1, q2_new, q2_full, q3_full, v3_full, lse_cach
     q1 against q2_full with the concatenated (lse23, msg). No causal mask, as
     in the reference when a cache is given. Returns (out, lse23_step, msg_step).
     """
-    cm1, cm2 = context_mask if _exists(context_mask) else (None, None)
+    cm1, cm2 = _propagate_masks(context_mask) if _exists(context_mask) else (None, None)
     msg_step, lse_step = pass_fwd(q2_new, q3_full, v3_full, softclamp=softclamp_value, key_mask=cm2)
     lse = lse_step if lse_cache is None else torch.cat((lse_cache.float(), lse_step), -1)
     msg = msg_step if msg_cache is None else torch.cat((msg_cache, msg_step), -2)
@@ -237,7 +254,7 @@ def poly_attention_chain(q_left, q_right, vs, *, softclamp_value=None, causal=Fa
     msgs in the reference's cache order.
     """
     order = len(q_left)
-    cms = tuple(context_masks) if context_masks is not None else (None,) * order
+    cms = _propagate_masks(context_masks) if context_masks is not None else (None,) * order
     q_left, q_right, vs = list(_autocast(*q_left)), list(_autocast(*q_right)), list(_autocast(*vs))
     res = _Chain.apply(order, softclamp_value, bool(causal), mask, cms, *q_left, *q_right, *vs)
     return res[0], res[1:order], res[order:]
@@ -253,7 +270,7 @@ def poly_attention_chain_cached(q_left, q_right_full, vs_full, cache_lses, cache
     new_msg_steps) in the reference's cache order.
     """
     order = len(q_left)
-    cms = tuple(context_masks) if context_masks is not None else (None,) * order
+    cms = _propagate_masks(context_masks) if context_masks is not None else (None,) * order
     val, vmul, bias = vs_full[-1], None, None
     step_lses, step_msgs = [], []
     for t in range(order - 1, 0, -1):

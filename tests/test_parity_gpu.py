@@ -388,3 +388,22 @@ def test_pass_bwd_other_head_dims(dtype, d):
     assert_close(dq, e[0], dtype, "dq")
     assert_close(dk, group(e[1]), dtype, "dk")
     assert_close(dv, group(e[2]), dtype, "dv")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_order2_pass1_mask_fully_masking_a_sequence(causal):
+    """context_mask = (None, cm2) with one sequence fully masked in pass 1:
+    its lse23 rows are -finfo.max, so pass 2 sees only dead keys there and must
+    give the reference's uniform average (the routing sends pass 2 to the
+    masked-pass kernels)."""
+    import poly_attention_b200 as P
+    dtype = torch.bfloat16
+    b, h, n, d = 2, 2, 96, 64
+    q1, q2, q3, v3 = (quant(rnd((b, h, n, d), s), dtype) for s in (31, 32, 33, 34))
+    cm2 = np.ones((b, n), dtype=bool)
+    cm2[1] = False
+    cm2[0, 40:] = False
+    out, _, _ = P.poly_attention_order2(dev(q1, dtype), dev(q2, dtype), dev(q3, dtype), dev(v3, dtype),
+                                        context_mask=(None, torch.as_tensor(cm2).cuda()), causal=causal)
+    eo, _, _ = O.order2_fwd(q1, q2, q2, q3, v3, context_mask=(None, cm2), causal=causal)
+    assert_close(out, eo, dtype, "out")
