@@ -191,7 +191,7 @@ def run_ours(args, rank, world, local_rank):
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
-            k2 = max(1, min(args.steps, 5))
+            k2 = max(3, min(args.steps, 10))
             s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s2.record()
             for _ in range(k2):

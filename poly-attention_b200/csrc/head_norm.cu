@@ -50,12 +50,14 @@ __global__ void __launch_bounds__(256) head_rmsnorm_kernel(const Norms P) {
       int k = 0;
       while (k + 1 < P.n && r >= P.start[k + 1]) ++k;
       const PolyHeadNorm& d = P.d[k];
-      const int64_t local = ok ? r - P.start[k] : 0;
-      const int64_t ni = local % d.rows, t = local / d.rows;
-      const int64_t hi = t % d.heads, bi = t / d.heads;
+      // row coordinates in 32-bit arithmetic (a tensor has < 2^31 rows)
+      const int local = ok ? (int)(r - P.start[k]) : 0;
+      const int t = local / d.rows, ni = local - t * d.rows;
+      const int bi = t / d.heads, hi = t - bi * d.heads;
       kd[u] = ok ? k : -1;
-      src[u] = (const TS*)d.src + bi * d.src_stride[0] + hi * d.src_stride[1] + ni * d.src_stride[2];
-      dst_row[u] = ((bi * d.heads + hi) * d.rows + ni) * d.dim;
+      src[u] = (const TS*)d.src + (int64_t)bi * d.src_stride[0] + (int64_t)hi * d.src_stride[1] +
+               (int64_t)ni * d.src_stride[2];
+      dst_row[u] = (int64_t)local * d.dim;
     }
 #pragma unroll
     for (int u = 0; u < NR; ++u) {
@@ -168,6 +170,7 @@ int head_rmsnorm(const PolyHeadNorm* norms, int n, cudaStream_t s) {
         (d.weight_dtype != d.src_dtype && d.weight_dtype != POLY_F32))
       return bad(at + "dst / weight dtype must be the source dtype or F32");
     if (d.batch < 0 || d.heads < 0 || d.rows < 0) return bad(at + "negative extent");
+    if ((int64_t)d.batch * d.heads * d.rows >= (int64_t)1 << 31) return bad(at + "more than 2^31 - 1 rows");
     const int esz = d.src_dtype == POLY_F32 ? 4 : 2;
     if (d.dim <= 0 || d.dim > 256 || d.dim % 8) return bad(at + "dim must be a multiple of 8 in [8, 256]");
     const int64_t cnt = (int64_t)d.batch * d.heads * d.rows;

@@ -32,8 +32,8 @@ def test_head_rmsnorm_matches_rmsnorm(dt, d, eps):
     for g, nm, x in zip(got, norms, xs):
         ref = nm(x)
         assert g.dtype == ref.dtype and g.shape == ref.shape and g.is_contiguous()
-        tol = 1e-5 if dt == torch.float32 else 1e-2
-        torch.testing.assert_close(g.float(), ref.float(), atol=tol, rtol=tol)
+        atol, rtol = (1e-5, 1e-5) if dt == torch.float32 else (2e-2, 1e-2)   # 16-bit: rounding order
+        torch.testing.assert_close(g.float(), ref.float(), atol=atol, rtol=rtol)
 
 
 def test_head_rmsnorm_autocast_and_fp32_weights():
