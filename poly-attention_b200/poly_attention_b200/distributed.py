@@ -14,8 +14,8 @@ Forward (causal, reference semantics of poly_attention/poly_attention.py:48-116)
    of the own rows, complete: pass-1 rows are exactly pass-2 keys.
 3. pass 2, key split: for each own key chunk c, the queries of chunk c
    (causal) and of every later chunk (no mask) attend keys c with lse23 as key
-   bias -> partial (out, lse) for every query row; the two own chunks are
-   merged locally (poly_lse_merge).
+   bias, as one causal call -> partial (out, lse) for every query row; the two
+   own chunks are merged locally (poly_lse_merge).
 4. the one exchange: all-reduce(max) of the partial lse per row, each rank
    rescales its partial by exp(lse - max), then reduce-scatter(sum) of
    [acc | l] (fp32) delivers every row's totals to its owner, which divides.
@@ -104,19 +104,19 @@ def context_parallel_order2_fwd(q1_loc, q2_loc, q3_loc, v3_loc, *, group=None, s
         msgs.append(o_d)
         lses.append(l_d)
 
-    # 3. pass 2 partials for every query row from the own key chunks
-    part_out = torch.zeros(2, b, h, n, d, device=q1.device, dtype=q1.dtype)
-    part_lse = torch.full((2, b, h, n), -math.inf, device=q1.device, dtype=torch.float32)
+    # 3. pass 2 partials for every query row from the own key chunks. Queries
+    # from chunk c on against keys of chunk c is one causal call: with both
+    # index ranges starting at c * C, the top-left causal rule masks exactly
+    # the diagonal block and leaves the later rows unmasked.
+    part_out = torch.empty(2, b, h, n, d, device=q1.device, dtype=q1.dtype)
+    part_lse = torch.empty(2, b, h, n, device=q1.device, dtype=torch.float32)
     for k, c in enumerate(own):
         q2c = q2_loc[:, :, k * C:(k + 1) * C]
-        o, l = pass_fn(rows(q1, c), q2c, msgs[k], causal=True, softclamp=softclamp_value, bias=lses[k])
-        part_out[k, :, :, c * C:(c + 1) * C] = o
-        part_lse[k, :, :, c * C:(c + 1) * C] = l
-        if c + 1 < 2 * world:
-            o, l = pass_fn(q1[:, :, (c + 1) * C:], q2c, msgs[k], causal=False, softclamp=softclamp_value,
-                           bias=lses[k])
-            part_out[k, :, :, (c + 1) * C:] = o
-            part_lse[k, :, :, (c + 1) * C:] = l
+        o, l = pass_fn(q1[:, :, c * C:], q2c, msgs[k], causal=True, softclamp=softclamp_value, bias=lses[k])
+        part_out[k, :, :, c * C:] = o
+        part_lse[k, :, :, c * C:] = l
+        part_out[k, :, :, :c * C] = 0        # rows before chunk c see none of its keys
+        part_lse[k, :, :, :c * C] = -math.inf
     out_p, lse_p = merge_fn(part_out, part_lse)
 
     # 4. exchange: max of lse, then sum of rescaled [acc | l] to the row owners
