@@ -64,15 +64,16 @@ template <typename T, int D, bool HAS_BIAS, bool SOFTCLAMP>
 __global__ void __launch_bounds__(256) pass_small_kernel(const PolyPassArgs a) {
   constexpr int KS = D / 16, NB = D / 8, CH = D / 8;
   constexpr int KNB = kMaxN / 8;   // key n-blocks
+  const int nq = a.seq_q, nk = a.seq_k;
+  const int kp = (nk + 15) & ~15;   // keys padded to the P.V K step
+  // shared memory sized to the keys present: K [kp][D], V [kp][D], bias [kp]
   extern __shared__ __align__(16) uint8_t sm[];
-  const uint32_t sK = tc::smem_u32(sm), sV = sK + kMaxN * D * 2;
-  float* sB = reinterpret_cast<float*>(sm + 2 * kMaxN * D * 2);
+  const uint32_t sK = tc::smem_u32(sm), sV = sK + kp * D * 2;
+  float* sB = reinterpret_cast<float*>(sm + 2 * kp * D * 2);
 
   const int bh = blockIdx.x;
   const int b = bh / a.heads, h = bh - b * a.heads;
   const int g = h / (a.heads / a.kv_heads);
-  const int nq = a.seq_q, nk = a.seq_k;
-  const int kp = (nk + 15) & ~15;   // keys padded to the P.V K step
   const T* kg = (const T*)a.k + b * a.k_stride[0] + g * a.k_stride[1];
   const T* vg = (const T*)a.v + b * a.v_stride[0] + g * a.v_stride[1];
   for (int c = threadIdx.x; c < kp * CH; c += blockDim.x) {
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(256) pass_small_kernel(const PolyPassArgs a) {
         ++count;
 #pragma unroll
         for (int n = 0; n < NB; ++n) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(sm + kMaxN * D * 2 + soff<D>(j, n) + 4 * tq);
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(sm + kp * D * 2 + soff<D>(j, n) + 4 * tq);
           const T* e = reinterpret_cast<const T*>(&w);
           o[n][2 * hf] += to_f32(e[0]);
           o[n][2 * hf + 1] += to_f32(e[1]);
@@ -238,7 +239,9 @@ int launch_t(const PolyPassArgs& a, cudaStream_t s) {
   });
   if (err != cudaSuccess) return cuda_status(err, "cudaFuncSetAttribute(small)");
   const int threads = 32 * ((a.seq_q + 15) / 16);
-  pass_small_kernel<T, D, B, C><<<a.batch * a.heads, threads, smem, s>>>(a);
+  const int kp = (a.seq_k + 15) & ~15;
+  const int bytes = 2 * kp * D * 2 + kp * 4;   // <= smem (the attribute's maximum)
+  pass_small_kernel<T, D, B, C><<<a.batch * a.heads, threads, bytes, s>>>(a);
   note_launch(1);
   return cuda_status(cudaGetLastError(), "pass_small launch");
 }
