@@ -277,16 +277,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (use_bias) ++nbias;
       const bool diag = p.causal && (j == mt);
       float tmax = -INFINITY;
+      // without softclamp or bias the scale is folded into the exponent's FFMA
+      const bool fold = !SOFTCLAMP && !use_bias;
       if (SOFTCLAMP) {
 #pragma unroll
         for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(tanhf(__uint_as_float(v[c]) * p.sc_in) * p.sc_out);
-      } else {
+        if (use_bias) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * p.sl2);
-      }
-      if (use_bias) {
+          for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) + bt[c]);
+        }
+      } else if (use_bias) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) + bt[c]);
+        for (int c = 0; c < BN; ++c) v[c] = __float_as_uint(fmaf(__uint_as_float(v[c]), p.sl2, bt[c]));
       }
       if (diag) {
 #pragma unroll
@@ -295,18 +297,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
 #pragma unroll
       for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, __uint_as_float(v[c]));
-      const float m_new = fmaxf(m_run, tmax);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = ex2(m_run - m_use);
+      if (fold) tmax *= p.sl2;
+      // lazy max: the running max (and O in TMEM) moves only when a row's max
+      // grows by more than 2^8; exponentials stay <= 2^8, exact in fp32 sums
+      float alpha = 1.f;
+      if (tmax > m_run + 8.f) {
+        alpha = ex2(m_run - tmax);
+        m_run = tmax;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       float sum = 0.f;
+      if (fold) {
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const float e = ex2(__uint_as_float(v[c]) - m_use);
-        sum += e;
-        v[c] = __float_as_uint(e);
+        for (int c = 0; c < BN; ++c) {
+          const float e = ex2(fmaf(__uint_as_float(v[c]), p.sl2, -m_use));
+          sum += e;
+          v[c] = __float_as_uint(e);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const float e = ex2(__uint_as_float(v[c]) - m_use);
+          sum += e;
+          v[c] = __float_as_uint(e);
+        }
       }
       l_run = l_run * alpha + sum;
-      m_run = m_new;
       if (j > 0) {
         // PV_{j-1} must be complete before O is rescaled and P is overwritten
         if (!mbar_wait_warp(o_done, (j - 1) & 1, abort_flag, err, 28)) { ok = false; break; }
