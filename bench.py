@@ -176,7 +176,9 @@ def run_ours(args, rank, world, local_rank):
                                         chunk=args.e2e_chunk)
 
         def e2e_streamed():
-            streamer.step(*hosts, grads=grads_h)
+            # consecutive steps overlap (the next step's inputs stream in while
+            # this one finishes); the timed region ends after join()
+            streamer.step(*hosts, grads=grads_h, sync=False)
 
         def e2e_autograd():
             d_in = [h.to(dev, non_blocking=True) for h in hosts]
@@ -186,8 +188,10 @@ def run_ours(args, rank, world, local_rank):
             for gh, tt in zip(grads_h, ts):
                 gh.copy_(tt.grad, non_blocking=True)
 
-        def timed(fn):
+        def timed(fn, finish=None):
             fn()
+            if finish:
+                finish()
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
@@ -196,6 +200,8 @@ def run_ours(args, rank, world, local_rank):
             s2.record()
             for _ in range(k2):
                 fn()
+            if finish:
+                finish()
             e2.record()
             torch.cuda.synchronize()
             te = torch.tensor([s2.elapsed_time(e2) / k2], device=dev)
@@ -204,7 +210,7 @@ def run_ours(args, rank, world, local_rank):
             return b * N * world / (float(te.item()) * 1e-3)
 
         h2d, d2h = streamer.bytes_per_step()
-        e2e = {"value": timed(e2e_streamed), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+        e2e = {"value": timed(e2e_streamed, streamer.join), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "api": f"HostStreamedOrder2.step (chunk {args.e2e_chunk})",
                "autograd_serial": {"value": timed(e2e_autograd), "unit": "tokens/s",
                                    "api": "flash_poly_attention + backward, copies before / after"}}

@@ -44,6 +44,8 @@ class HostStreamedOrder2:
         self._s_d2h = torch.cuda.Stream(self.device)
         self._in_ready = [torch.cuda.Event() for _ in range(slots)]
         self._in_free = [torch.cuda.Event() for _ in range(slots)]
+        self._used = [False] * slots   # slot k has an earlier chunk whose compute must finish first
+        self._next = 0                 # next slot (continues across steps)
 
     def _compute(self, q1, q2, q3, v3, do):
         sc, causal = self.softclamp, self.causal
@@ -55,13 +57,16 @@ class HostStreamedOrder2:
                                   dq_accumulate=True)
         return out, (dq1, dq2, dq3, dv3)
 
-    def step(self, q1, q2, q3, v3, dout, grads=None, out=None):
+    def step(self, q1, q2, q3, v3, dout, grads=None, out=None, sync=True):
         """One forward + backward. Inputs: host tensors [b, h|g, n, d] (pinned
         for overlap). Gradients (dq1, dq2, dq3, dv3) are written into `grads`
         (host tensors, allocated pinned if None) and, if `out` is given, the
         forward output into it. Work is enqueued after everything already on
-        the current stream, and the current stream waits for it, so events /
-        synchronisation on the current stream cover the whole step."""
+        the current stream. With sync=True the current stream then waits for
+        the step, so events / synchronisation on it cover the whole step. With
+        sync=False it does not: the next step's copies in start while this
+        step's last chunks compute and copy out (steps overlap like a
+        prefetching loader); call join() before reading the outputs."""
         hosts = (q1, q2, q3, v3, dout)
         for x in hosts:
             if x.is_cuda:
@@ -73,11 +78,13 @@ class HostStreamedOrder2:
             s.wait_stream(cur)
         C = self.chunk
         for c in range(self.b // C):
-            k = c % self.slots
+            k = self._next
+            self._next = (self._next + 1) % self.slots
             sl = slice(c * C, (c + 1) * C)
             with torch.cuda.stream(self._s_h2d):
-                if c >= self.slots:
+                if self._used[k]:
                     self._s_h2d.wait_event(self._in_free[k])
+                self._used[k] = True
                 for dst, src in zip(self._in[k], hosts):
                     dst.copy_(src[sl], non_blocking=True)
                 self._in_ready[k].record(self._s_h2d)
@@ -93,9 +100,15 @@ class HostStreamedOrder2:
                 if out is not None:
                     out[sl].copy_(o, non_blocking=True)
                     o.record_stream(self._s_d2h)
+        if sync:
+            self.join()
+        return grads
+
+    def join(self):
+        """Make the current stream wait for every step enqueued so far."""
+        cur = torch.cuda.current_stream(self.device)
         cur.wait_stream(self._s_d2h)
         cur.wait_stream(self._s_h2d)
-        return grads
 
     def bytes_per_step(self):
         """(host-to-device, device-to-host) bytes of one step (gradients only)."""

@@ -36,3 +36,24 @@ def test_host_streamed_refuses_device_tensors():
     x = torch.zeros(1, 1, 64, 64, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         st.step(x, x, x, x, x)
+
+
+def test_host_streamed_overlapping_steps():
+    """sync=False steps overlap across step boundaries (slots are reused only
+    after their previous chunk computed); after join() every step's gradients
+    equal those of synchronous steps."""
+    import poly_attention_b200 as P
+    b, h, n, d, dt = 4, 2, 256, 64, torch.bfloat16
+    gen = torch.Generator().manual_seed(6)
+    batches = [[torch.randn(b, h, n, d, generator=gen).to(dt).pin_memory() for _ in range(5)] for _ in range(3)]
+    st = P.HostStreamedOrder2(batch=b, heads=h, kv_heads=h, seq_len=n, dim_head=d, chunk=1, slots=2)
+    outs = [[torch.empty(b, h, n, d, dtype=dt).pin_memory() for _ in range(4)] for _ in batches]
+    for x, g in zip(batches, outs):
+        st.step(*x, grads=g, sync=False)
+    st.join()
+    torch.cuda.synchronize()
+    for x, g in zip(batches, outs):
+        ref = st.step(*x)
+        torch.cuda.synchronize()
+        for a, r in zip(g, ref):
+            torch.testing.assert_close(a.float(), r.float(), atol=2e-2, rtol=1e-2)
