@@ -19,6 +19,7 @@
 //   TMEM -> swizzled fp32 smem -> TMA reduce-add into the fp32 accumulator
 // A preprocessing kernel forms delta_i = dout_i . out_i - dlse_i and the
 // log2-domain lse; a final kernel converts the fp32 dq accumulator.
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -464,6 +465,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+#include "bwd2_body.cuh"
+
 // delta_i = dout_i . out_i - dlse_i and nlse2_i = -lse_i * log2(e), padded to
 // nq_pad rows per (batch, head) with (delta 0, nlse2 -inf) so padded queries
 // get p = 0. Eight lanes per row, 16-byte loads.
@@ -563,14 +566,30 @@ BwdWs bwd_ws(const PolyPassBwdArgs& a) {
   return w;
 }
 
+// POLY_BWD_TWO_TILE=1 selects the two-tile pipelined kernel (bwd2_body.cuh):
+// correct, but slower than pass_bwd_tc_kernel at config 2 (1.50 vs 1.37 ms
+// per pass), so it is opt-in.
+bool bwd_two_tile() {
+  static const bool v = [] {
+    const char* e = getenv("POLY_BWD_TWO_TILE");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 template <typename T, bool SOFTCLAMP, bool HAS_BIAS, bool DB>
 int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   using L = BwdLayout;
+  constexpr bool kTwo = !SOFTCLAMP;   // the two-tile kernel has no softclamp path
+  const bool two = kTwo && bwd_two_tile();
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS, DB>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (attr_err == cudaSuccess && kTwo)
+      attr_err = cudaFuncSetAttribute(pass_bwd_tc2_kernel<T, HAS_BIAS, DB>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, Bwd2Layout::kAlloc);
   });
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "cudaFuncSetAttribute(bwd tc)");
   const PolyPassArgs& f = a.fwd;
@@ -615,7 +634,10 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   p.dbias_stride[1] = a.dbias_stride[1];
   p.k_tiles = (f.seq_k + BK - 1) / BK;
   dim3 grid(p.k_tiles * f.batch * f.kv_heads);
-  pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS, DB><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
+  if (two)
+    pass_bwd_tc2_kernel<T, HAS_BIAS, DB><<<grid, kThreads, Bwd2Layout::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
+  else
+    pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS, DB><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
   const int64_t cthreads = (int64_t)f.batch * f.heads * f.seq_q * (D / 8);
   bwd_dq_convert_kernel<T><<<(unsigned)((cthreads + 255) / 256), 256, 0, s>>>(a, w.dq_acc);
   note_launch(3);
