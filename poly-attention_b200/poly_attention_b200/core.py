@@ -163,6 +163,7 @@ def poly_attention_order2(q1, q2, q3, v3, *, q2_pass1=None, mask=None, context_m
     return out, lse23, msg
 
 
+@torch.compiler.disable
 def poly_attention_order2_cached(q1, q2_new, q2_full, q3_full, v3_full, lse_cache, msg_cache, *,
                                  softclamp_value=None, context_mask=None, mask=None):
     """One KV-cache step of order 2 (poly_attention/poly_attention.py:84-87,
@@ -246,6 +247,7 @@ class _Chain(torch.autograd.Function):
         return (None, None, None, None, None, *dql, *dqr, *dvs)
 
 
+@torch.compiler.disable   # the chain / cached cores run eagerly under torch.compile
 def poly_attention_chain(q_left, q_right, vs, *, softclamp_value=None, causal=False, mask=None, context_masks=None):
     """Order-n chain without cache (n = len(q_left)).
 
@@ -260,6 +262,7 @@ def poly_attention_chain(q_left, q_right, vs, *, softclamp_value=None, causal=Fa
     return res[0], res[1:order], res[order:]
 
 
+@torch.compiler.disable
 def poly_attention_chain_cached(q_left, q_right_full, vs_full, cache_lses, cache_msgs, *, softclamp_value=None,
                                 mask=None, context_masks=None):
     """One KV-cache step of the order-n chain (n_poly_attention.py:265-313).

@@ -88,6 +88,7 @@ def _fill_pass(a: PolyPassArgs, q, k, v, out, lse, *, causal, softclamp, scale, 
     keep.extend([q, k, v, bias, key_mask, query_mask, epi_mul, v_mul])
 
 
+@torch.compiler.disable   # library calls through ctypes: dynamo runs them eagerly
 def pass_fwd(q, k, v, *, causal=False, softclamp=None, scale=None, bias=None, key_mask=None, query_mask=None,
              epi_mul=None, v_mul=None, out=None, lse=None, want_lse=True):
     """One attention pass (see PolyPassArgs in include/poly_attention.h).
@@ -122,6 +123,7 @@ def pass_fwd(q, k, v, *, causal=False, softclamp=None, scale=None, bias=None, ke
     return out, lse
 
 
+@torch.compiler.disable
 def pass_bwd(q, k, v, out, lse, dout, *, causal=False, softclamp=None, scale=None, bias=None, key_mask=None,
              query_mask=None, dlse=None, dq=None, dq_accumulate=False, want_dbias=False):
     """Backward of ``pass_fwd``. Returns (dq, dk, dv, dbias-or-None)."""
@@ -157,6 +159,7 @@ def pass_bwd(q, k, v, out, lse, dout, *, causal=False, softclamp=None, scale=Non
     return dq, dk, dv, dbias
 
 
+@torch.compiler.disable
 def kernel_names(q, k, v, *, causal=False, bias=None, key_mask=None, query_mask=None):
     """(forward, backward) kernel family the library picks for these inputs."""
     a = PolyPassBwdArgs()
@@ -174,6 +177,7 @@ def kernel_names(q, k, v, *, causal=False, bias=None, key_mask=None, query_mask=
             lib.poly_pass_bwd_kernel_name(ctypes.byref(a)).decode())
 
 
+@torch.compiler.disable
 def lse_merge(part_out, part_lse):
     """Merge key-split partials: part_out [P, ..., d], part_lse [P, ...] -> (out, lse)."""
     _require_cuda(part_out, part_lse)

@@ -38,3 +38,23 @@ def test_compiled_module_under_autocast_matches_eager(causal):
     assert not torch.isnan(oc).any()
     torch.testing.assert_close(oc.float(), oe.float(), atol=2e-2, rtol=1e-2)
     torch.testing.assert_close(xc.grad, xe.grad, atol=2e-2, rtol=1e-2)
+
+
+def test_compiled_npoly_under_autocast_matches_eager():
+    """The order-n module compiles (the chain core is an autograd Function:
+    dynamo treats its library calls as graph breaks) and matches eager."""
+    from poly_attention_b200 import NPolyAttention
+    torch.manual_seed(1)
+    attn = NPolyAttention(dim=128, order=3, heads=4, kv_heads=2, dim_head=64, causal=True).cuda()
+    x = torch.randn(2, 96, 128, device="cuda")
+    xe, xc = x.clone().requires_grad_(True), x.clone().requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        oe = attn(xe)
+        oe.float().sum().backward()
+    torch._dynamo.reset()
+    model = torch.compile(attn)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        oc = model(xc)
+        oc.float().sum().backward()
+    torch.testing.assert_close(oc.float(), oe.float(), atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(xc.grad, xe.grad, atol=2e-2, rtol=1e-2)
