@@ -1,4 +1,4 @@
-// tcgen05 forward pass, head_dim 64, two 128-query tiles per CTA (sm_100a).
+// tcgen05 forward pass, head_dim 64 or 128, two 128-query tiles per CTA (sm_100a).
 //
 // Same maths as pass_fwd_tc_kernel (pass_tc100.cu), organised so the tensor
 // core never waits on one softmax warpgroup: a CTA owns query rows
@@ -36,14 +36,17 @@ int read_device_error_fwd2(int* out, bool reset) {
 namespace {
 using namespace tc;
 
-constexpr int D = 64;
 constexpr int BM = 128;   // rows per tile (two tiles per CTA)
 constexpr int BN = 128;   // keys per stage
-constexpr int S = 3;      // K / V stages
 constexpr int kThreads = 384;
 
-struct L2 {
-  static constexpr int kTile = 128 * D * 2;   // 16 KB
+// D = 64: 3 K / V stages, P in its own TMEM columns. D = 128: 2 stages, P
+// written over the first 64 columns of its own S buffer (TMEM holds S_A, S_B,
+// O_A, O_B at 128 columns each), so S(j + 1) is issued after P V(j).
+template <int D>
+struct L2T {
+  static constexpr int S = D == 64 ? 3 : 2;
+  static constexpr int kTile = 128 * D * 2;   // one [128][D] 16-bit tile (D / 64 swizzle atoms)
   static constexpr int kQ = 0;                // 2 tiles
   static constexpr int kK = kQ + 2 * kTile;   // S stages
   static constexpr int kV = kK + S * kTile;
@@ -95,11 +98,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
-template <typename T, bool HAS_BIAS>
+template <typename T, bool HAS_BIAS, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     pass_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_b,
                         const Fwd2Params p) {
+  using L2 = L2T<D>;
+  constexpr int S = L2::S;
+  constexpr bool kAlias = D == 128;   // P over the first half of its S buffer
+  constexpr int kAtom = 128 * 128;     // bytes of one 64-column swizzle atom of a 128-row tile
   constexpr int kIsBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -161,17 +168,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
       mbar_arrive_expect_tx(q_full, 2 * L2::kTile);
-      tma_load_4d(sQ, &tm_q, q_full, 0, row0, h, b);
-      tma_load_4d(sQ + L2::kTile, &tm_q, q_full, 0, row0 + BM, h, b);
+#pragma unroll
+      for (int hf = 0; hf < D / 64; ++hf) {
+        tma_load_4d(sQ + hf * kAtom, &tm_q, q_full, hf * 64, row0, h, b);
+        tma_load_4d(sQ + L2::kTile + hf * kAtom, &tm_q, q_full, hf * 64, row0 + BM, h, b);
+      }
       int issued = 0;
       for (int j = 0; j < ntMax; ++j) {
         const int s = j % S;
         if (j >= S && !mbar_wait(&kv_empty[s], ((j / S) - 1) & 1, abort_flag, err, 41)) break;
         mbar_arrive_expect_tx(&k_full[s], L2::kTile + (HAS_BIAS ? BN * 4 : 0));
-        tma_load_4d(sK + s * L2::kTile, &tm_k, &k_full[s], 0, j * BN, kvh, b);
+#pragma unroll
+        for (int hf = 0; hf < D / 64; ++hf)
+          tma_load_4d(sK + s * L2::kTile + hf * kAtom, &tm_k, &k_full[s], hf * 64, j * BN, kvh, b);
         if (HAS_BIAS) tma_load_3d(sB + s * BN, &tm_b, &k_full[s], j * BN, kvh, b);
         mbar_arrive_expect_tx(&v_full[s], L2::kTile);
-        tma_load_4d(sV + s * L2::kTile, &tm_v, &v_full[s], 0, j * BN, kvh, b);
+#pragma unroll
+        for (int hf = 0; hf < D / 64; ++hf)
+          tma_load_4d(sV + s * L2::kTile + hf * kAtom, &tm_v, &v_full[s], hf * 64, j * BN, kvh, b);
         issued = j + 1;
       }
       if (*abort_flag) {
@@ -191,16 +205,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_s = [&](int x, int j) {
         const int s = j % S;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_f16_ss(tmem + x * BN, smem_desc_sw128(qa + x * L2::kTile + kk * 32, 16, 1024),
-                     smem_desc_sw128(ka + s * L2::kTile + kk * 32, 16, 1024), idS, kk > 0);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t koff = (uint32_t)(kk >> 2) * kAtom + (uint32_t)(kk & 3) * 32;
+          mma_f16_ss(tmem + x * BN, smem_desc_sw128(qa + x * L2::kTile + koff, 16, 1024),
+                     smem_desc_sw128(ka + s * L2::kTile + koff, 16, 1024), idS, kk > 0);
+        }
         mma_commit(&s_full[x]);
       };
       auto issue_pv = [&](int x, int j) {
         const int s = j % S;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_f16_ts(tmem + 256 + x * D, tmem + 384 + x * 64 + kk * 8,
+          mma_f16_ts(tmem + 256 + x * D, tmem + (kAlias ? x * BN : 384 + x * 64) + kk * 8,
                      smem_desc_sw128(va + s * L2::kTile + kk * 2048, BN * 128, 1024), idO, (j > 0 || kk > 0));
         mma_commit(&o_done[x]);
       };
@@ -221,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int x = 0; x < 2; ++x) {
           const int nt = x == 0 ? ntA : ntB;
           if (j >= nt) continue;
-          if (j + 1 < nt) {
+          if (!kAlias && j + 1 < nt) {
             if (!(ok = mbar_wait(&s_free[x], j & 1, abort_flag, err, 45))) break;
             tc_fence_after();
             issue_s(x, j + 1);
@@ -233,6 +249,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           issue_pv(x, j);
+          // aliased P: S(j + 1) overwrites P(j); MMAs of one issuer run in order,
+          // so P V(j) has read P before S(j + 1) writes those columns
+          if (kAlias && j + 1 < nt) issue_s(x, j + 1);
         }
         if (!ok) break;
         mma_commit(&kv_empty[s]);
@@ -249,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int diag_tile = 2 * mt + x;             // causal: the key tile on this tile's diagonal
     const uint32_t s_addr = tmem + lane_base + x * BN;
     const uint32_t o_addr = tmem + lane_base + 256 + x * D;
-    const uint32_t p_addr = tmem + lane_base + 384 + x * 64;
+    const uint32_t p_addr = tmem + lane_base + (kAlias ? x * BN : 384 + x * 64);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
@@ -261,8 +280,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_free[x]);                  // S is in registers: the MMA may overwrite it
+      if (!kAlias) {
+        tc_fence_before();
+        mbar_arrive(&s_free[x]);                // S is in registers: the MMA may overwrite it
+      }
       const bool tail = (j == kt_total - 1) && (p.seq_k % BN) != 0;
       const bool diag = p.causal && (j == diag_tile);
       float tmax = -INFINITY;
@@ -394,12 +415,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, L2::kTmemCols);
 }
 
-template <typename T, bool HAS_BIAS>
+template <typename T, bool HAS_BIAS, int D>
 int launch_t(const PolyPassArgs& a, cudaStream_t st) {
+  using L2 = L2T<D>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(pass_fwd_tc2_kernel<T, HAS_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(pass_fwd_tc2_kernel<T, HAS_BIAS, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     L2::kAlloc);
   });
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "cudaFuncSetAttribute(fwd tc2)");
@@ -443,28 +465,35 @@ int launch_t(const PolyPassArgs& a, cudaStream_t st) {
   p.lse_stride[0] = a.lse_stride[0];
   p.lse_stride[1] = a.lse_stride[1];
   dim3 grid(a.batch * a.heads, p.m_tiles);
-  pass_fwd_tc2_kernel<T, HAS_BIAS><<<grid, kThreads, L2::kAlloc, st>>>(tq, tk, tv, tb, p);
+  pass_fwd_tc2_kernel<T, HAS_BIAS, D><<<grid, kThreads, L2::kAlloc, st>>>(tq, tk, tv, tb, p);
   note_launch(1);
   return cuda_status(cudaGetLastError(), "pass_fwd_tc2 launch");
 }
 
 }  // namespace
 
-// d = 64, no softclamp (the two-tile kernel keeps 128 scores per thread in
-// registers; softclamp's tanh goes to the one-tile kernel), bias rows usable
-// by TMA (16-byte aligned base and strides).
+// d = 64 or 128, no softclamp (the two-tile kernel keeps 128 scores per
+// thread in registers; softclamp's tanh goes to the one-tile kernel), bias
+// rows usable by TMA (16-byte aligned base and strides).
 bool pass_fwd_tc2_eligible(const PolyPassArgs& a) {
-  if (a.head_dim != D || a.softclamp > 0.f) return false;
+  if ((a.head_dim != 64 && a.head_dim != 128) || a.softclamp > 0.f) return false;
   if (a.bias && (!aligned16(a.bias) || (a.bias_stride[0] & 3) || (a.bias_stride[1] & 3) || a.bias_stride[0] <= 0 ||
                  a.bias_stride[1] <= 0))
     return false;
   return true;
 }
 
-int launch_pass_fwd_tc2(const PolyPassArgs& a, cudaStream_t s) {
+namespace {
+template <int D>
+int launch_d(const PolyPassArgs& a, cudaStream_t s) {
   if (a.dtype == POLY_BF16)
-    return a.bias ? launch_t<__nv_bfloat16, true>(a, s) : launch_t<__nv_bfloat16, false>(a, s);
-  return a.bias ? launch_t<__half, true>(a, s) : launch_t<__half, false>(a, s);
+    return a.bias ? launch_t<__nv_bfloat16, true, D>(a, s) : launch_t<__nv_bfloat16, false, D>(a, s);
+  return a.bias ? launch_t<__half, true, D>(a, s) : launch_t<__half, false, D>(a, s);
+}
+}  // namespace
+
+int launch_pass_fwd_tc2(const PolyPassArgs& a, cudaStream_t s) {
+  return a.head_dim == 128 ? launch_d<128>(a, s) : launch_d<64>(a, s);
 }
 
 }  // namespace poly
