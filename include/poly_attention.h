@@ -168,7 +168,9 @@ POLY_API int poly_lse_merge(const PolyMergeArgs* args, void* stream);
  * its CTAs start while the previous pass drains, stream every key tile but the
  * last, and wait for the previous pass before loading the last. Every pass
  * must take the decode kernel (poly_pass_fwd_kernel_name() == "decode"), else
- * POLY_EUNSUPPORTED and nothing is launched. No workspace is used.
+ * POLY_EUNSUPPORTED and nothing is launched. A pass with few (batch, kv head)
+ * groups needs a workspace of poly_pass_fwd_workspace_size() bytes (0 otherwise);
+ * a pass given too little gets POLY_EINVAL and nothing is launched.
  */
 POLY_API int poly_decode_chain(const PolyPassArgs* passes, int n, void* stream);
 

@@ -136,6 +136,12 @@ int poly_decode_chain(const PolyPassArgs* passes, int n, void* stream) {
     if (passes[i].seq_q != 1 || choose_fwd(passes[i]) != FwdKind::kDecode)
       return fail(POLY_EUNSUPPORTED, "poly_decode_chain: pass " + std::to_string(i) + " does not take the decode kernel");
   }
+  for (int i = 0; i < n; ++i) {
+    const size_t need = pass_decode_workspace(passes[i]);
+    if (need && (!passes[i].workspace || passes[i].workspace_bytes < need))
+      return fail(POLY_EINVAL, "poly_decode_chain: pass " + std::to_string(i) + " needs a workspace of " +
+                                   std::to_string(need) + " bytes");
+  }
   cudaStream_t s = (cudaStream_t)stream;
   for (int i = 0; i < n; ++i) {
     const int rc = launch_pass_decode(passes[i], s, i > 0);

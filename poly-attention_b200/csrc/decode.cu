@@ -28,7 +28,9 @@
 // trips. The four warp states are merged through shared memory, then the
 // cluster's CTA records are merged through distributed shared memory, and the
 // cluster writes out, lse and the optional epilogue product: no partials go
-// through HBM and no second kernel runs.
+// through HBM and no second kernel runs. With few groups (one long sequence)
+// a global-split mode runs up to 64 splits per group instead and merges their
+// records with a small combine kernel (workspace, see global_splits).
 #include <cooperative_groups.h>
 
 #include <cfloat>
@@ -51,6 +53,8 @@ constexpr int kWarps = 4;
 constexpr int kWarpKeys = 16;                 // keys per warp per stage (one m16n8k16 K step of P.V)
 constexpr int kTile = kWarps * kWarpKeys;     // keys per stage
 constexpr int kMaxSplits = 8;                 // portable cluster size
+constexpr int kMaxGlobalSplits = 64;          // splits per group in the global-split mode
+constexpr int kMinGlobalTiles = 16;           // key tiles per split, at least, in that mode
 constexpr int kThreads = (kWarps + 1) * 32;  // warps 0..3 consume, warp 4 produces
 
 // Shared memory: ring [stage][array (k, v, v_mul)][64 keys x D] (1024-byte
@@ -154,7 +158,7 @@ template <typename T, int D, int R, bool HAS_BIAS, bool HAS_VMUL, bool SOFTCLAMP
 __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_constant__ CUtensorMap tm_k,
                                                                const __grid_constant__ CUtensorMap tm_v,
                                                                const __grid_constant__ CUtensorMap tm_m,
-                                                               const PolyPassArgs a, int kps) {
+                                                               const PolyPassArgs a, int kps, float* part) {
   constexpr int NARR = HAS_VMUL ? 3 : 2;
   constexpr int NST = num_stages<D, NARR>();
   constexpr int SB = stage_bytes<D, NARR>();
@@ -371,6 +375,13 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
       crec[rr * (D + 2) + 1] = ls;
     }
   }
+  if (part) {
+    // global-split mode: the CTA record goes to the workspace for the combine kernel
+    __syncthreads();
+    float* dstp = part + ((int64_t)group * gridDim.x + split) * R * (D + 2);
+    for (int i = threadIdx.x; i < R * (D + 2); i += kThreads) dstp[i] = crec[i];
+    return;
+  }
   cluster.sync();   // CTA records visible to the whole cluster
 
   // cluster merge: CTA `split` writes its share of the group's R x D outputs
@@ -427,6 +438,89 @@ int read_device_error_dec(int* out, bool reset) {
 
 namespace {
 
+// Global-split mode: one CTA per (group, query head of the group) merges the
+// `nsp` CTA records of the row. The records' weights go to shared memory
+// first; then 8 slices of 32 threads each sum every 8th record over the
+// features (independent loads, so the records stream in parallel rather than
+// one L2 round trip per record), the slices add up in shared memory, and the
+// CTA writes out, lse and the epilogue product as the cluster path does.
+constexpr int kCombThreads = 256, kCombSlices = kCombThreads / 32;
+
+template <typename T, int D, int R, bool HAS_VMUL>
+__global__ void __launch_bounds__(kCombThreads) decode_combine_kernel(const PolyPassArgs a, const float* part,
+                                                                       int nsp) {
+  __shared__ float sf[kMaxGlobalSplits], sl[kMaxGlobalSplits];
+  __shared__ float red[kCombSlices][D];
+  __shared__ float sM, sL;
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, slice = tid >> 5;
+  const int group = row / R, rr = row - group * R;
+  const int b = group / a.kv_heads, g = group - b * a.kv_heads, h = g * R + rr;
+  auto rec = [&](int sp) { return part + (((int64_t)group * nsp + sp) * R + rr) * (D + 2); };
+  // the split kernel's records are complete once the primary grid is
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (tid < nsp) {
+    sf[tid] = rec(tid)[0];
+    sl[tid] = rec(tid)[1];
+  }
+  __syncthreads();
+  if (slice == 0) {
+    float m = -INFINITY;
+    for (int sp = lane; sp < nsp; sp += 32) m = fmaxf(m, sf[sp]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int sp = lane; sp < nsp; sp += 32) l += sf[sp] == -INFINITY ? 0.f : sl[sp] * exp2f(sf[sp] - m);
+    l = warp_sum(l);
+    __syncwarp();
+    for (int sp = lane; sp < nsp; sp += 32) sf[sp] = sf[sp] == -INFINITY ? 0.f : exp2f(sf[sp] - m);
+    if (lane == 0) {
+      sM = m;
+      sL = l;
+    }
+  }
+  __syncthreads();
+  float o[D / 32];
+#pragma unroll
+  for (int t = 0; t < D / 32; ++t) o[t] = 0.f;
+#pragma unroll 4
+  for (int sp = slice; sp < nsp; sp += kCombSlices) {
+    const float f = sf[sp];
+    const float* r = rec(sp) + 2;
+#pragma unroll
+    for (int t = 0; t < D / 32; ++t) o[t] = fmaf(r[lane + 32 * t], f, o[t]);
+  }
+#pragma unroll
+  for (int t = 0; t < D / 32; ++t) red[slice][lane + 32 * t] = o[t];
+  __syncthreads();
+  if (tid >= D) return;
+  const int c = tid;
+  const float M = sM, L = sL;
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < kCombSlices; ++k) acc += red[k][c];
+  float inv = L > 0.f ? 1.f / L : 0.f, lse_v = (M + __log2f(L)) * kLn2;
+  if (M == -INFINITY) {
+    // every key dead: the reference's uniform average of the values, lse = -FLT_MAX
+    const T* vg = (const T*)a.v + b * a.v_stride[0] + g * a.v_stride[1];
+    const T* mg = HAS_VMUL ? (const T*)a.v_mul + b * a.v_mul_stride[0] + g * a.v_mul_stride[1] : nullptr;
+    acc = 0.f;
+    for (int j = 0; j < a.seq_k; ++j) {
+      float vv = to_f32(vg[(int64_t)j * a.v_stride[2] + c]);
+      if (HAS_VMUL) vv = to_f32(from_f32<T>(vv * to_f32(mg[(int64_t)j * a.v_mul_stride[2] + c])));
+      acc += vv;
+    }
+    inv = a.seq_k > 0 ? 1.f / (float)a.seq_k : 0.f;
+    lse_v = -FLT_MAX;
+  }
+  const T ov = from_f32<T>(acc * inv);
+  ((T*)a.out)[b * a.out_stride[0] + h * a.out_stride[1] + c] = ov;
+  if (a.epi_out) {
+    const T em = ((const T*)a.epi_mul)[b * a.epi_mul_stride[0] + h * a.epi_mul_stride[1] + c];
+    ((T*)a.epi_out)[b * a.epi_out_stride[0] + h * a.epi_out_stride[1] + c] = from_f32<T>(to_f32(em) * to_f32(ov));
+  }
+  if (a.lse && c == 0) a.lse[b * a.lse_stride[0] + h * a.lse_stride[1]] = lse_v;
+}
+
 struct DecodeGeom {
   int splits, kps;  // key splits (cluster size) and keys per split
 };
@@ -449,6 +543,46 @@ DecodeGeom geometry(const PolyPassArgs& a, int slots) {
   gm.kps = max(kTile, ((a.seq_k + splits - 1) / splits + kTile - 1) / kTile * kTile);
   gm.splits = max(1, (a.seq_k + gm.kps - 1) / gm.kps);
   return gm;
+}
+
+// Global-split mode, for few (batch, kv head) groups (e.g. one long sequence):
+// clusters of <= kMaxSplits CTAs cannot fill the GPU there, so up to
+// kMaxGlobalSplits splits per group write their CTA records to the workspace
+// and a combine kernel merges them. The choice and the split count depend on
+// the SM count only, so the workspace size and the launch agree.
+
+int sm_count() {
+  static std::mutex mu;
+  static int sms_dev[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!sms_dev[dev]) {
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    sms_dev[dev] = max(1, sms);
+  }
+  return sms_dev[dev];
+}
+
+// splits of the global-split mode, or 0 when the cluster path is used: the
+// mode is taken only where it gives more splits than a cluster can hold, with
+// every split still streaming >= kMinGlobalTiles tiles (fewer, and the
+// pipeline ramp-up of each CTA costs more than the extra CTAs gain) and the
+// whole grid inside one wave of two CTAs per SM
+int global_splits(const PolyPassArgs& a) {
+  const int groups = max(1, a.batch * a.kv_heads);
+  const int ntiles = (a.seq_k + kTile - 1) / kTile;
+  const int target = 2 * sm_count();
+  static const bool off = [] {                // POLY_DECODE_GLOBAL=0: cluster path only (tuning)
+    const char* e = getenv("POLY_DECODE_GLOBAL");
+    return e && e[0] == '0';
+  }();
+  if (off) return 0;
+  const int want = min(kMaxGlobalSplits, min(ntiles / kMinGlobalTiles, target / groups));
+  if (want <= kMaxSplits) return 0;
+  const int kps = ((a.seq_k + want - 1) / want + kTile - 1) / kTile * kTile;
+  return (a.seq_k + kps - 1) / kps;
 }
 
 // (batch, kv head, row) strides for a tensor map: the stride of an extent-1
@@ -485,7 +619,14 @@ int launch_one(const PolyPassArgs& a, cudaStream_t s, bool dependent) {
     }
     slots = slots_dev[dev];
   }
-  const DecodeGeom gm = geometry(a, slots);
+  DecodeGeom gm = geometry(a, slots);
+  const int gsp = global_splits(a);
+  float* part = nullptr;
+  if (gsp > 0) {
+    gm.splits = gsp;
+    gm.kps = ((a.seq_k + gsp - 1) / gsp + kTile - 1) / kTile * kTile;
+    part = (float*)a.workspace;
+  }
   CUtensorMap tk, tv, tm;
   const int rows = max(a.seq_k, 1);   // seq_k == 0 issues no load
   int64_t ks[3], vs[3], ms[3];
@@ -506,15 +647,27 @@ int launch_one(const PolyPassArgs& a, cudaStream_t s, bool dependent) {
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = gm.splits;
+  attr[0].val.clusterDim.x = part ? 1 : gm.splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = dependent ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<T, D, R, B, V, C>, tk, tv, tm, a, gm.kps);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<T, D, R, B, V, C>, tk, tv, tm, a, gm.kps, part);
   note_launch(1);
+  if (e == cudaSuccess && part) {
+    // programmatic dependent of the split kernel: it waits (griddepcontrol)
+    // for the records, and lets the next pass of a chain start its prologue
+    cudaLaunchConfig_t cc = {};
+    cc.gridDim = dim3(a.batch * a.kv_heads * R);
+    cc.blockDim = dim3(kCombThreads);
+    cc.stream = s;
+    cc.attrs = &attr[1];
+    cc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cc, decode_combine_kernel<T, D, R, V>, a, (const float*)part, gm.splits);
+    note_launch(1);
+  }
   return cuda_status(e, "decode launch");
 }
 
@@ -561,7 +714,15 @@ bool pass_decode_eligible(const PolyPassArgs& a) {
 }
 
 // partials never leave the cluster: no workspace
-size_t pass_decode_workspace(const PolyPassArgs&) { return 0; }
+// partials go through the workspace only in the global-split mode
+size_t pass_decode_workspace(const PolyPassArgs& a) {
+  // A fixed bound (the most splits any length can take) rather than this
+  // length's split count: once a cache is long enough for the global mode it
+  // stays there as it grows, so a workspace sized at the cache's capacity
+  // covers every shorter length too.
+  if (!global_splits(a)) return 0;
+  return (size_t)a.batch * a.kv_heads * kMaxGlobalSplits * (a.heads / a.kv_heads) * (a.head_dim + 2) * sizeof(float);
+}
 
 int launch_pass_decode(const PolyPassArgs& a, cudaStream_t s, bool dependent) {
   if (a.dtype == POLY_BF16)

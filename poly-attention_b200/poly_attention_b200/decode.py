@@ -62,6 +62,7 @@ class ChainDecoder:
         self._args = {}
         self._ws = {}
         self._chain = None           # poly_decode_chain usable (decided on the first step)
+        self._ws_ready = False
         for t in range(order - 1, -1, -1):
             a = self._arr[order - 1 - t]
             a.batch, a.kv_heads, a.head_dim = batch, kv_heads, dim_head
@@ -142,6 +143,15 @@ class ChainDecoder:
                 a.q, a.q_stride = q1_new.data_ptr(), _st3(q1_new)
                 a.out, a.out_stride = out.data_ptr(), _st3(out)
                 a.lse = None
+        if not self._ws_ready:
+            # few (batch, kv head) groups take the global-split decode, which
+            # needs a workspace; size it once for the full capacity (the largest need)
+            for t in range(self.order - 1, -1, -1):
+                a = self._args[t]
+                a.seq_k = self.cap
+                self._workspace(t, a)
+                a.seq_k = n
+            self._ws_ready = True
         if self._chain is not False:
             rc = lib.poly_decode_chain(self._arr, self.order, stream)
             if rc == _lib.POLY_OK:

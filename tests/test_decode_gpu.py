@@ -218,3 +218,66 @@ def test_decode_fully_dead_keys(vmul):
     eo_, el = O.pass_fwd(q, np.repeat(k, r, 1), np.repeat(vv, r, 1), bias=np.repeat(bias, r, 1))
     np.testing.assert_allclose(host(out), eo_, atol=ATOL, rtol=RTOL)
     np.testing.assert_allclose(host(lse), el, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("extras", ["none", "bias+vmul+epi", "dead"])
+@pytest.mark.parametrize("b,h,g,L,d", [(1, 8, 2, 20000, 128), (1, 4, 4, 12000, 64), (2, 16, 2, 12000, 128)])
+def test_decode_global_split(b, h, g, L, d, extras):
+    """Few (batch, kv head) groups and long caches take the global-split mode
+    (up to 64 splits per group, CTA records merged by a combine kernel)."""
+    import poly_attention_b200 as P
+    dt = torch.bfloat16
+    q = host(dev(rnd((b, h, 1, d), 31), dt))
+    k, v, vm = (host(dev(rnd((b, g, L, d), s), dt)) for s in (32, 33, 34))
+    em = host(dev(rnd((b, h, 1, d), 35), dt))
+    bias = rnd((b, g, L), 36)
+    kw, vv, obias = {}, v, None
+    if extras == "dead":
+        bias[0] = -np.finfo(np.float32).max
+    if extras != "none":
+        kw["bias"], obias = dev(bias, torch.float32), np.repeat(bias, h // g, 1)
+    if "vmul" in extras:
+        kw["v_mul"] = dev(vm, dt)
+        vv = host(dev(v * vm, dt))
+    qt, kt, vt = dev(q, dt), dev(k, dt), dev(v, dt)
+    assert P.kernel_names(qt, kt, vt)[0] == "decode"
+    from poly_attention_b200 import _lib
+    n0 = _lib.launch_count()
+    if "epi" in extras:
+        out, lse, eo = P.pass_fwd(qt, kt, vt, epi_mul=dev(em, dt), **kw)
+    else:
+        out, lse = P.pass_fwd(qt, kt, vt, **kw)
+    assert _lib.launch_count() - n0 == 2   # split kernel + combine kernel
+    r = h // g
+    eo_, el = O.pass_fwd(q, np.repeat(k, r, 1), np.repeat(vv, r, 1), bias=obias)
+    np.testing.assert_allclose(host(out), eo_, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(host(lse), el, atol=ATOL, rtol=RTOL)
+    if "epi" in extras:
+        np.testing.assert_allclose(host(eo), em * host(out), atol=ATOL, rtol=RTOL)
+
+
+def test_chain_decoder_single_sequence_long_cache():
+    """Batch 1 through ChainDecoder (global-split levels inside poly_decode_chain)
+    equals the level-by-level launches."""
+    from poly_attention_b200.decode import ChainDecoder
+    dt = torch.bfloat16
+    b, order, h, g, d, L0, steps = 1, 3, 16, 4, 128, 12000, 6
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    decs = [ChainDecoder(batch=b, order=order, heads=h, kv_heads=g, dim_head=d, capacity=L0 + steps + 8, dtype=dt)
+            for _ in range(2)]
+    for bufs in zip(*[dd.qs + dd.vs + dd.msgs + dd.lses for dd in decs]):
+        bufs[0][:, :, :L0].normal_(generator=gen)
+        bufs[1].copy_(bufs[0])
+    for dd in decs:
+        dd.length = L0
+    decs[1]._chain = False
+    for _ in range(steps):
+        qn = [torch.randn(b, g, 1, d, device="cuda", dtype=dt, generator=gen) for _ in range(order)]
+        vn = [torch.randn(b, g, 1, d, device="cuda", dtype=dt, generator=gen) for _ in range(order - 1)]
+        q1 = torch.randn(b, h, 1, d, device="cuda", dtype=dt, generator=gen)
+        outs = []
+        for dd in decs:
+            dd.append_kv(qn, vn)
+            outs.append(dd.step(q1).clone())
+        assert torch.equal(outs[0], outs[1])
+    assert decs[0]._chain is True
