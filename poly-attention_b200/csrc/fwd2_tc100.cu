@@ -61,7 +61,7 @@ struct L2T {
 
 struct Fwd2Params {
   int seq_q, seq_k, heads, kv_heads, m_tiles, causal;
-  float sl2;
+  float sl2, scale;
   void* out; int64_t out_stride[3];
   float* lse; int64_t lse_stride[2];
   const void* epi_mul; int64_t epi_mul_stride[3];
@@ -288,22 +288,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool diag = p.causal && (j == diag_tile);
       float tmax = -INFINITY;
       // Without a bias the row max is taken on the raw scores and the scale is
-      // folded into the exponent's FFMA; with a bias x = s * scale * log2e + b
-      // is formed first. Both end with v[] holding values whose 2^(v*mul - m)
-      // is the unnormalised probability.
-      float mul = 1.f;
+      // folded into the exponent's FFMA; with a bias x = s * scale + b (natural
+      // units, one FFMA) is formed first and log2(e) folded into the exponent's
+      // FFMA instead. Both end with v[] holding values whose 2^(v*mul - m) is
+      // the unnormalised probability.
+      float mul = p.sl2;
       if (HAS_BIAS) {
+        mul = kLog2e;
         const float4* b4 = reinterpret_cast<const float4*>(sB + s * BN);
 #pragma unroll
         for (int q = 0; q < BN / 4; ++q) {
           const float4 bb = b4[q];
-          v[4 * q + 0] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 0]), p.sl2, bb.x * kLog2e));
-          v[4 * q + 1] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 1]), p.sl2, bb.y * kLog2e));
-          v[4 * q + 2] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 2]), p.sl2, bb.z * kLog2e));
-          v[4 * q + 3] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 3]), p.sl2, bb.w * kLog2e));
+          v[4 * q + 0] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 0]), p.scale, bb.x));
+          v[4 * q + 1] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 1]), p.scale, bb.y));
+          v[4 * q + 2] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 2]), p.scale, bb.z));
+          v[4 * q + 3] = __float_as_uint(fmaf(__uint_as_float(v[4 * q + 3]), p.scale, bb.w));
         }
-      } else {
-        mul = p.sl2;
       }
       if (tail) {
         const int kvalid = p.seq_k - j * BN;
@@ -453,6 +453,7 @@ int launch_t(const PolyPassArgs& a, cudaStream_t st) {
   p.m_tiles = (a.seq_q + 2 * BM - 1) / (2 * BM);
   p.causal = a.causal;
   p.sl2 = a.scale * kLog2e;
+  p.scale = a.scale;
   p.out = a.out;
   p.lse = a.lse;
   p.epi_mul = a.epi_mul;
