@@ -264,12 +264,14 @@ def run_decode(args, dev):
     """Config 4 decode: NPolyAttention order 3 core, batch 32, 16 query / 4 kv
     heads, d 128, bf16; caches of 2048 positions (synthetic N(0,1) contents
     stand in for the prefill), then 256 single-token steps through
-    ChainDecoder (in-place cache appends + one decode kernel pair per level)."""
+    ChainDecoder (in-place cache appends + one decode launch per level).
+    --decode-batch / --decode-cache change batch and prefilled length (e.g.
+    one sequence with a 131072-position cache, the global-split mode)."""
     import torch
 
     from poly_attention_b200 import _lib
     from poly_attention_b200.decode import ChainDecoder
-    b, h, g, d, order, L0 = 32, 16, 4, 128, 3, 2048
+    b, h, g, d, order, L0 = args.decode_batch, 16, 4, 128, 3, args.decode_cache
     steps = 256 if args.workload != "decode" else max(1, args.steps)
     dec = ChainDecoder(batch=b, order=order, heads=h, kv_heads=g, dim_head=d, capacity=L0 + steps + 8,
                        dtype=torch.bfloat16, device=dev)
@@ -302,7 +304,8 @@ def run_decode(args, dev):
     _, _, hbm, kind = peaks()
     gbs = total_bytes / (ms * 1e-3) / 1e9
     return {"metric": "decode tok/s", "value": b * steps / (ms * 1e-3), "unit": "tokens/s", "steps": steps,
-            "ms_per_step": ms / steps, "config": {"workload": "NPolyAttention order 3 core decode (config 4)",
+            "ms_per_step": ms / steps, "config": {"workload": "NPolyAttention order 3 core decode (config 4)"
+                                                  if (b, L0) == (32, 2048) else "NPolyAttention order 3 core decode",
                                                   "batch": b, "heads": h, "kv_heads": g, "dim_head": d,
                                                   "cache_len": f"{L0 + 1}..{L0 + steps}"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
@@ -464,6 +467,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--e2e-chunk", type=int, default=1, help="batch elements per streamed chunk (e2e leg)")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
+    ap.add_argument("--decode-batch", type=int, default=32, help="decode leg batch (config 4: 32)")
+    ap.add_argument("--decode-cache", type=int, default=2048, help="decode leg prefilled cache length (config 4: 2048)")
     ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4", "decode"], default="train",
                     help="train: config 2 fwd+bwd (the headline); longctx: config 5 key-split forward")
     args = ap.parse_args()
