@@ -56,27 +56,69 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML
+    queries every 10 ms from a background thread (read-only; the GPU is found
+    by the CUDA device's UUID), or nvidia-smi every 200 ms where NVML is not
+    usable. A timed region of tens of milliseconds gets several samples."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.lines = []
+        self.samples = []          # (sm_mhz, max_mhz, reasons) from NVML
+        self.source = None
+        self._stop = None
+        self._thread = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(self.index).uuid)
+        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
+
+    def _nvml_loop(self, pynvml, hdl):
+        bits = [getattr(pynvml, "nvmlClocksEventReason" + n, None) for n in
+                ("HwSlowdown", "HwThermalSlowdown", "SwThermalSlowdown", "SwPowerCap")]
+        mx = pynvml.nvmlDeviceGetMaxClockInfo(hdl, pynvml.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(hdl, pynvml.NVML_CLOCK_SM)
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(hdl)
+                self.samples.append((sm, mx, [n for n, bt in zip(self.NAMES, bits) if bt is not None and r & bt]))
+            except Exception:  # noqa: BLE001 - a failed query only loses a sample
+                pass
+            self._stop.wait(0.01)
 
     def __enter__(self):
+        import threading
+        try:
+            pynvml, hdl = self._nvml_handle()
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._nvml_loop, args=(pynvml, hdl), daemon=True)
+            self._thread.start()
+            self.source = "nvml 10 ms"
+            return self
+        except Exception:  # noqa: BLE001 - NVML absent or unusable: nvidia-smi instead
+            self._thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi 200 ms"
         except OSError:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -88,7 +130,10 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s_mhz, m_mhz, rs in self.samples:
+            sm.append(float(s_mhz))
+            mx = float(m_mhz)
+            reasons.update(rs)
         for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
@@ -98,11 +143,11 @@ class ClockSampler:
                 mx = float(f[2])
             except ValueError:
                 continue
-            for nm, v in zip(names, f[5:9]):
+            for nm, v in zip(self.NAMES, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": self.source}
 
 
 def make_inputs(device, seed, b):
