@@ -1,9 +1,9 @@
 """Generate golden vectors by running the reference implementation itself.
 
-Run in a container that has the reference checkout (read-only) at
-``$POLY_REFERENCE`` (default ``/root/reference``):
+Run where a checkout of lucidrains/poly-attention (read-only) is available,
+with ``POLY_REFERENCE`` naming its directory:
 
-    python tests/golden/make_golden.py
+    POLY_REFERENCE=<checkout> python tests/golden/make_golden.py
 
 The three dependencies the reference imports but this image lacks (einx,
 torch-einops-utils, rotary-embedding-torch) are replaced by the test-only
@@ -33,7 +33,9 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("POLY_REFERENCE", "/root/reference")
+REF = os.environ.get("POLY_REFERENCE")
+if not REF or not os.path.isdir(os.path.join(REF, "poly_attention")):
+    sys.exit("set POLY_REFERENCE to a checkout of lucidrains/poly-attention (the directory holding poly_attention/)")
 sys.path.insert(0, os.path.join(HERE, "shims"))
 sys.path.insert(0, REF)
 
