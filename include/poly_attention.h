@@ -240,7 +240,10 @@ POLY_API int poly_pass_bwd_noalloc(const PolyPassBwdArgs* args, void* stream);
 POLY_API size_t poly_noalloc_scratch_bytes(void);
 
 /* Name of the kernel family poly_pass_fwd / poly_pass_bwd would launch for
- * these arguments ("tc100" tcgen05 path, "simt" CUDA-core path, "decode"). */
+ * these arguments: forward "decode" (one query row against a cache), "small"
+ * (short sequences, mma.sync), "tf32x3" (fp32 on tensor cores), "tc100"
+ * (tcgen05) or "simt" (CUDA cores); backward "tc100" or "simt"; "invalid"
+ * when the arguments fail validation. */
 POLY_API const char* poly_pass_fwd_kernel_name(const PolyPassArgs* args);
 POLY_API const char* poly_pass_bwd_kernel_name(const PolyPassBwdArgs* args);
 
