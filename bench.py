@@ -119,6 +119,11 @@ class ClockSampler:
         if self._thread is not None:
             self._stop.set()
             self._thread.join(timeout=5)
+            try:
+                import pynvml
+                pynvml.nvmlShutdown()
+            except Exception:  # noqa: BLE001 - shutdown failure changes nothing measured
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
