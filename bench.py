@@ -9,13 +9,27 @@ pass 1 backward, over synthetic N(0, 1) inputs resident in HBM (4 inputs + dO,
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU (torchrun, one rank per GPU): every rank runs the full per-GPU
-workload on its own batch (batch x head sharding, no collective), so total
-work grows with N ("weak"); time is the max over ranks.
+The default line also carries, as sub-objects, the other BASELINE configs
+measured on the same GPU (config 1 module fp32 forward, config 3 PolyViT,
+config 4 prefill and decode, config 5 long-context forward), each with its
+own clock record and roofline fraction, the reference's own Triton kernel
+timed on the same inputs (``triton_reference``, run in a child process), and
+``cpu_baseline``: the reference's torch CPU path on one sequence of the
+bench's own inputs, whose results also check the GPU's for that sequence.
 
-The reference arm (--impl reference) times the CPU restatement of the
-reference algorithm (oracle/poly_oracle.py, numpy, all host threads) on a
-bounded sample: one (batch, head) unit of the same workload per step.
+Multi-GPU (torchrun, one rank per GPU): every rank runs the full per-GPU
+config-2 workload on its own batch (batch x head sharding, no collective), so
+total work grows with N ("weak"); time is the max over ranks and ``value`` is
+the aggregate over all ranks. The line then also carries the config-5 leg:
+the n = 32768 forward with its keys split across the N ranks (one NCCL
+exchange), total work fixed ("strong").
+
+The reference arm (--impl reference) times the reference's own CPU torch
+path (``reference_poly_attention`` from the unmodified package copied to
+baseline/_ref, run with the test-only shims for its three absent
+dependencies) on all host threads, fp32, forward + backward on a bounded
+sample of the config-2 workload per step (one sequence, as many of its 16
+heads as keep the run within a few minutes).
 """
 from __future__ import annotations
 
@@ -32,6 +46,8 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "poly-attention_b200"))
 
 METRIC = "order-2 poly-attn fwd+bwd tokens/s/GPU @4K ctx (% bf16 peak); decode tok/s"
+# `value` is the aggregate over all GPUs of the job; `value_per_gpu` divides by N.
+UNIT = "tokens/s (all GPUs)"
 B, H, N, D = 8, 16, 4096, 64
 
 
@@ -75,12 +91,18 @@ class ClockSampler:
         self._stop = None
         self._thread = None
 
+    def _uuid(self):
+        import torch
+        return "GPU-" + str(torch.cuda.get_device_properties(self.index).uuid)
+
     def _nvml_handle(self):
         import pynvml
-        import torch
         pynvml.nvmlInit()
-        uuid = "GPU-" + str(torch.cuda.get_device_properties(self.index).uuid)
-        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        try:
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(self._uuid())
+        except Exception:
+            pynvml.nvmlShutdown()   # init succeeded: release it before falling back
+            raise
 
     def _nvml_loop(self, pynvml, hdl):
         bits = [getattr(pynvml, "nvmlClocksEventReason" + n, None) for n in
@@ -107,7 +129,8 @@ class ClockSampler:
         except Exception:  # noqa: BLE001 - NVML absent or unusable: nvidia-smi instead
             self._thread = None
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+            # nvidia-smi numbers GPUs in PCI order, ignoring CUDA_VISIBLE_DEVICES: select by UUID
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self._uuid()}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.source = "nvidia-smi 200 ms"
@@ -162,7 +185,8 @@ def make_inputs(device, seed, b):
 
 
 def step_device(P, q1, q2, q3, v3, do, ev=None):
-    """One forward + backward of both passes through the library's pass API."""
+    """One forward + backward of both passes through the library's pass API.
+    Returns (out, dq1, dq2, dq3, dv3)."""
     if ev is not None:
         ev[0].record()
     msg, lse23 = P.pass_fwd(q2, q3, v3, causal=True)
@@ -171,12 +195,36 @@ def step_device(P, q1, q2, q3, v3, do, ev=None):
     out, lse12 = P.pass_fwd(q1, q2, msg, causal=True, bias=lse23)
     if ev is not None:
         ev[2].record()
-    _, dq2, dmsg, dlse23 = P.pass_bwd(q1, q2, msg, out, lse12, do, causal=True, bias=lse23, want_dbias=True)
+    dq1, dq2, dmsg, dlse23 = P.pass_bwd(q1, q2, msg, out, lse12, do, causal=True, bias=lse23, want_dbias=True)
     if ev is not None:
         ev[3].record()
-    P.pass_bwd(q2, q3, v3, msg, lse23, dmsg, causal=True, dlse=dlse23, dq=dq2, dq_accumulate=True)
+    _, dq3, dv3, _ = P.pass_bwd(q2, q3, v3, msg, lse23, dmsg, causal=True, dlse=dlse23, dq=dq2, dq_accumulate=True)
     if ev is not None:
         ev[4].record()
+    return out, dq1, dq2, dq3, dv3
+
+
+def timed_region(fn, steps, dev, world, local_rank):
+    """K calls of fn between two CUDA events on the current stream, barrier and
+    synchronize on both sides, clocks sampled during; returns (ms per call,
+    max over ranks; clock summary)."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), clk.summary()
 
 
 def run_ours(args, rank, world, local_rank):
@@ -213,6 +261,15 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
+
+    # results of one more (untimed) step, sequence 0: checked against the
+    # reference's CPU path in the cpu_baseline leg
+    sample = None
+    if world == 1 and not args.no_cpu:
+        res = step_device(P, q1, q2, q3, v3, do)
+        sample = {"inputs": [x[:1].float().cpu() for x in (q1, q2, q3, v3, do)],
+                  "gpu": [x[:1].float().cpu() for x in res]}
+        del res
 
     # end to end through the public API: host (pinned) inputs in, gradients out.
     # Headline: HostStreamedOrder2 (batch chunks streamed, PCIe both ways
@@ -260,11 +317,24 @@ def run_ours(args, rank, world, local_rank):
             return b * N * world / (float(te.item()) * 1e-3)
 
         h2d, d2h = streamer.bytes_per_step()
-        e2e = {"value": timed(e2e_streamed, streamer.join), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+        e2e = {"value": timed(e2e_streamed, streamer.join), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "api": f"HostStreamedOrder2.step (chunk {args.e2e_chunk})",
-               "autograd_serial": {"value": timed(e2e_autograd), "unit": "tokens/s",
+               "autograd_serial": {"value": timed(e2e_autograd), "unit": UNIT,
                                    "api": "flash_poly_attention + backward, copies before / after"}}
-    decode = None if args.no_decode else run_decode(args, dev)
+        del hosts, grads_h, streamer
+    del q1, q2, q3, v3, do
+    torch.cuda.empty_cache()
+
+    decode = None if args.no_decode or rank != 0 else run_decode(args, dev)
+    configs = {}
+    if not args.no_configs:
+        if world == 1:
+            for name in ("config1", "vit", "prefill4"):
+                configs[name] = run_module_config(name, args, dev, local_rank)
+                torch.cuda.empty_cache()
+        # config 5: one GPU alone, or keys split across all ranks (one NCCL exchange)
+        configs["longctx"] = run_longctx(args, rank, world, local_rank)
+        torch.cuda.empty_cache()
     if world > 1:
         dist.barrier()
     if rank != 0:
@@ -278,10 +348,12 @@ def run_ours(args, rank, world, local_rank):
     flops = [pf, pf, 2 * pf, 2 * pf]
     dom = max(range(4), key=lambda k: phases[k])
     achieved = flops[dom] / (phases[dom] * 1e-3) / 1e12
-    return {
+    value = b * N * world / (ms_step * 1e-3)
+    line = {
         "metric": METRIC,
-        "value": b * N * world / (ms_step * 1e-3),
-        "unit": "tokens/s",
+        "value": value,
+        "unit": UNIT,
+        "value_per_gpu": value / world,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
@@ -295,19 +367,24 @@ def run_ours(args, rank, world, local_rank):
                    "heads": H, "seq_len": N, "dim_head": D, "parallelism": f"dp{world} (batch x head sharding)",
                    "l2": "inputs (5 x 67 MB per GPU at batch 8) larger than L2; no flush"},
         "tflops": step_flop / (ms_step * 1e-3) / 1e12,
-        "frac_of_peak": step_flop / (ms_step * 1e-3) / 1e12 / sustained,
+        "frac_of_peak": step_flop / (ms_step * 1e-3) / 1e12 / burst,
         "phases_ms": dict(zip(names, phases)),
-        "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": sustained,
-                     "unit": "TFLOP/s", "frac": achieved / sustained,
+        "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": burst,
+                     "unit": "TFLOP/s", "frac": achieved / burst,
                      "traffic": TRAFFIC_PER_BATCH[names[dom]] * b,
                      "traffic_note": "ncu DRAM read+write bytes of a batch-1 capture x batch",
-                     "peak_kind": f"{kind} bf16 sustained"},
+                     "peak_kind": f"{kind} bf16 burst (timed region well under a second)"},
         "e2e": e2e,
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
-        "cpu_baseline": cpu_baseline() if (world == 1 and not args.no_cpu) else None,
         "decode": decode,
+        "configs": configs or None,
     }
+    if world == 1 and not args.no_triton:
+        line["triton_reference"] = triton_reference(args)
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(sample)
+    return line
 
 
 def run_decode(args, dev):
@@ -343,13 +420,15 @@ def run_decode(args, dev):
     total_bytes = 0
     n0 = _lib.launch_count()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        dec.append_kv(qn, vn)
-        dec.step(q1, out)
-        total_bytes += dec.bytes_per_step()
-    e.record()
-    torch.cuda.synchronize()
+    with ClockSampler(dev.index or 0) as clk:
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(steps):
+            dec.append_kv(qn, vn)
+            dec.step(q1, out)
+            total_bytes += dec.bytes_per_step()
+        e.record()
+        torch.cuda.synchronize()
     ms = s.elapsed_time(e)
     _, _, hbm, kind = peaks()
     gbs = total_bytes / (ms * 1e-3) / 1e9
@@ -361,114 +440,165 @@ def run_decode(args, dev):
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                          "traffic": None, "peak_kind": f"{kind} copy bandwidth",
                          "bytes_note": "7 bf16 cache tensors + 2 fp32 lse caches at kv-head width per position"},
-            "gpu_launches": int(_lib.launch_count() - n0)}
+            "clocks": clk.summary(), "gpu_launches": int(_lib.launch_count() - n0)}
+
+
+LONGCTX = (1, 16, 32768, 64)
 
 
 def run_longctx(args, rank, world, local_rank):
     """Config 5: order-2 causal forward, b1 h16 n32768 d64 bf16, keys split
-    across the ranks (zig-zag shards, one max all-reduce + one reduce-scatter of
-    fp32 partials); total work fixed ("strong" scaling)."""
+    across the ranks (zig-zag shards, see poly_attention_b200.distributed);
+    total work fixed ("strong" scaling). At one GPU the same code runs without
+    any collective."""
     import torch
-    import torch.distributed as dist
 
     from poly_attention_b200 import _lib
     from poly_attention_b200.distributed import context_parallel_order2_fwd, zigzag_shard
-    b, h, n, d = 1, 16, 32768, 64
+    b, h, n, d = LONGCTX
     dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(5)
     full = [torch.randn(b, h, n, d, device=dev, dtype=torch.bfloat16, generator=g) for _ in range(4)]
     loc = [zigzag_shard(t, rank, world).contiguous() for t in full]
     del full
     for _ in range(args.warmup):
         context_parallel_order2_fwd(*loc)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     n0 = _lib.launch_count()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(args.steps):
-        context_parallel_order2_fwd(*loc)
-    e.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([s.elapsed_time(e) / args.steps], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    if rank != 0:
-        return None
-    ms = float(t.item())
+    ms, clk = timed_region(lambda: context_parallel_order2_fwd(*loc), args.steps, dev, world, local_rank)
+    launches = _lib.launch_count() - n0
+    del loc
     flop = 2 * 2 * 2 * (n * n / 2) * d * h * b            # two causal passes
-    sustained, _, _, kind = peaks()
+    _, burst, _, kind = peaks()
+    tf = flop / (ms * 1e-3) / 1e12
     return {"metric": "long-context order-2 fwd ms (config 5)", "value": ms, "unit": "ms", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded",
+            "higher_is_better": False, "scaling": "strong", "dtype": "bf16", "data": "synthetic N(0,1), seeded",
             "config": {"workload": "order-2 causal fwd, keys split across GPUs", "batch": b, "heads": h,
                        "seq_len": n, "dim_head": d, "parallelism": f"cp{world} (zig-zag key split)"},
-            "tflops": flop / (ms * 1e-3) / 1e12, "frac_of_peak": flop / (ms * 1e-3) / 1e12 / (sustained * world),
-            "peak_kind": f"{kind} bf16 sustained x {world}", "gpu_launches_rank0": int(_lib.launch_count() - n0)}
+            "tflops": tf,
+            "roofline": {"bound": "tensor", "achieved": tf / world, "peak": burst, "unit": "TFLOP/s per GPU",
+                         "frac": tf / world / burst, "peak_kind": f"{kind} bf16 burst",
+                         "flop_note": "2 causal passes x 2 GEMMs x 2 n^2 d / 2 x heads"},
+            "clocks": clk, "gpu_launches_per_rank": int(launches / max(args.steps, 1))}
 
 
-def _time_module(fn, args, dev):
-    import torch
-    for _ in range(args.warmup):
-        fn()
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(args.steps):
-        fn()
-    e.record()
-    torch.cuda.synchronize()
-    return s.elapsed_time(e) / args.steps
-
-
-def run_module_configs(args, dev):
+def run_module_config(name, args, dev, local_rank):
     """Configs 1, 3 and the config-4 prefill through the drop-in modules
     (projections / norms / MLPs in PyTorch, attention cores in libpolyattn)."""
     import torch
 
     import poly_attention_b200 as P
+    from poly_attention_b200 import _lib
     torch.manual_seed(0)
-    out = {}
-    if args.workload == "config1":
+    sustained, burst, _, kind = peaks()
+    if name == "config1":
         m = P.PolyAttention(dim=512, heads=8, dim_head=64, causal=False).to(dev)
         x = torch.randn(1, 1024, 512, device=dev)
-        with torch.no_grad():
-            ms = _time_module(lambda: m(x), args, dev)
-        out = {"metric": "config 1 PolyAttention fp32 forward tokens/s", "value": 1024 / (ms * 1e-3),
-               "unit": "tokens/s", "ms_per_step": ms, "dtype": "f32",
+        fn, tokens, unit = (lambda: m(x)), 1024, "tokens/s"
+        flop, fl_note = 6.98e9, "core 4.295 GFLOP + projections 2.68 GFLOP"
+        out = {"metric": "config 1 PolyAttention fp32 forward tokens/s", "dtype": "f32",
                "config": {"workload": "PolyAttention(dim=512, heads=8, dim_head=64) fwd, x [1, 1024, 512]"}}
-    elif args.workload == "vit":
+        bound = "latency (one small fp32 forward; attention on 3xTF32 tensor-core passes)"
+    elif name == "vit":
         m = P.PolyViT(image_size=256, patch_size=32, num_classes=1000, dim=1024, depth=6, heads=16, dim_head=64,
                       mlp_dim=2048, order=2).to(dev, torch.bfloat16)
-        img = torch.randn(256, 3, 256, 256, device=dev, dtype=torch.bfloat16)
-        with torch.no_grad():
-            ms = _time_module(lambda: m(img), args, dev)
-        flop = 2.01e12
-        sustained, _, _, kind = peaks()
-        out = {"metric": "config 3 PolyViT bf16 forward images/s", "value": 256 / (ms * 1e-3), "unit": "images/s",
-               "ms_per_step": ms, "dtype": "bf16", "tflops": flop / (ms * 1e-3) / 1e12,
-               "frac_of_peak": flop / (ms * 1e-3) / 1e12 / sustained,
+        x = torch.randn(256, 3, 256, 256, device=dev, dtype=torch.bfloat16)
+        fn, tokens, unit = (lambda: m(x)), 256, "images/s"
+        flop, fl_note = 2.01e12, "whole model forward (linears 1.96e12 + attention core 5.15e10 + head)"
+        out = {"metric": "config 3 PolyViT bf16 forward images/s", "dtype": "bf16",
                "config": {"workload": "PolyViT(256/32, dim 1024, depth 6, heads 16, mlp 2048) fwd, batch 256",
                           "tokens": "64 patches (the reference has no cls token)"}}
-    elif args.workload == "prefill4":
+        bound = "tensor"
+    else:
         m = P.NPolyAttention(dim=2048, order=3, heads=16, kv_heads=4, dim_head=128, causal=True).to(
             dev, torch.bfloat16)
         x = torch.randn(32, 2048, 2048, device=dev, dtype=torch.bfloat16)
-        with torch.no_grad():
-            ms = _time_module(lambda: m(x), args, dev)
-        out = {"metric": "config 4 NPolyAttention order-3 GQA prefill tokens/s", "value": 32 * 2048 / (ms * 1e-3),
-               "unit": "tokens/s", "ms_per_step": ms, "dtype": "bf16",
+        fn, tokens, unit = (lambda: m(x)), 32 * 2048, "tokens/s"
+        flop, fl_note = 8.25e11, "attention core only (order 3, kv-side passes at 4 kv heads); projections excluded"
+        out = {"metric": "config 4 NPolyAttention order-3 GQA prefill tokens/s", "dtype": "bf16",
                "config": {"workload": "NPolyAttention(dim=2048 assumed, order 3, h16, g4, d128, causal) fwd, "
                                       "x [32, 2048, 2048]"}}
-    out.update({"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "data": "synthetic N(0,1), seeded",
-                "higher_is_better": True, "vs_baseline": None})
+        bound = "tensor"
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            fn()
+        n0 = _lib.launch_count()
+        ms, clk = timed_region(fn, args.steps, dev, 1, local_rank)
+        launches = _lib.launch_count() - n0
+    tf = flop / (ms * 1e-3) / 1e12
+    out.update({"value": tokens / (ms * 1e-3), "unit": unit, "ms_per_step": ms, "n_gpus": 1, "steps": args.steps,
+                "warmup": args.warmup, "data": "synthetic N(0,1), seeded; random-init weights",
+                "higher_is_better": True, "vs_baseline": None,
+                "roofline": {"bound": bound, "achieved": tf, "peak": burst, "unit": "TFLOP/s", "frac": tf / burst,
+                             "peak_kind": f"{kind} bf16 burst", "flop_note": fl_note},
+                "clocks": clk, "gpu_launches_per_step": int(launches / max(args.steps, 1))})
+    del m, x
     return out
 
 
-def cpu_unit_seconds():
-    """Oracle (numpy, fp32) forward + backward of one (batch, head) unit of the workload."""
+# ---------------------------------------------------------------- references
+
+def _reference_package():
+    """The reference's own modules: the unmodified package copied to
+    baseline/_ref (its pip build needs hatchling, absent offline), imported
+    with the test-only shims for einx / torch-einops-utils /
+    rotary-embedding-torch (tests/golden/shims: call-site patterns only)."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref, "poly_attention", "poly_attention.py")):
+        raise RuntimeError("baseline/_ref/poly_attention is missing (copy the reference package there)")
+    for p in (os.path.join(ROOT, "tests", "golden", "shims"), ref):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import poly_attention.poly_attention as refmod
+    return refmod
+
+
+def reference_cpu_step(refmod, ins):
+    """reference_poly_attention (poly_attention/poly_attention.py:48-116)
+    forward + autograd backward on CPU, fp32. ins = (q1, q2, q3, v3, dout)
+    [1, hs, N, D]. Returns (out, dq1, dq2, dq3, dv3)."""
+    import torch
+    q1, q2, q3, v3 = [x.detach().clone().requires_grad_(True) for x in ins[:4]]
+    out, _, _ = refmod.reference_poly_attention(q1, q2, q2, q3, v3, causal=True)
+    out.backward(ins[4])
+    with torch.no_grad():
+        return out.detach(), q1.grad, q2.grad, q3.grad, v3.grad
+
+
+def cpu_baseline(sample):
+    """The reference's torch CPU path on sequence 0 of the bench's own inputs
+    (all 16 heads, fp32 upcast: bf16 matmuls on CPU are not representative),
+    timed once on all host threads, and the GPU's results for that sequence
+    checked against it (bf16 vs fp32: max-abs 2e-2 + rel 1e-2)."""
+    import torch
+    torch.set_num_threads(os.cpu_count())
+    try:
+        refmod = _reference_package()
+    except Exception as exc:  # noqa: BLE001 - the port below stands in, labelled
+        return cpu_baseline_port(f"reference package unavailable: {exc}")
+    ins = sample["inputs"]
+    reference_cpu_step(refmod, [x[:, :1, :256] for x in ins])      # warm-up (allocator, threads)
+    t0 = time.perf_counter()
+    ref = reference_cpu_step(refmod, ins)
+    sec = time.perf_counter() - t0
+    names = ["out", "dq1", "dq2", "dq3", "dv3"]
+    parity = {}
+    ok = True
+    for nm, g, r in zip(names, sample["gpu"], ref):
+        err = (g - r).abs()
+        tol = 2e-2 + 1e-2 * r.abs()
+        ok &= bool((err <= tol).all())
+        parity[nm] = {"max_abs_err": float(err.max()), "max_excess_over_tol": float((err - tol).max())}
+    parity["pass"] = ok
+    parity["tolerance"] = "|gpu - ref| <= 2e-2 + 1e-2 |ref| elementwise, GPU bf16 vs reference fp32"
+    return {"value": N / sec, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"one sequence (16 heads) of the bench's inputs, seq {N}, fp32 torch CPU fwd+bwd of "
+                      f"reference_poly_attention, {sec:.2f} s",
+            "parity_vs_gpu": parity}
+
+
+def cpu_baseline_port(why):
+    """Fallback when the reference package is absent: the numpy restatement
+    (oracle/poly_oracle.py, BLAS matmuls) on one (batch, head) unit."""
     import numpy as np
 
     from oracle import poly_oracle as O
@@ -477,33 +607,107 @@ def cpu_unit_seconds():
     t0 = time.perf_counter()
     O.order2_fwd(a[0], a[1], a[1], a[2], a[3], causal=True)
     O.order2_bwd(a[0], a[1], a[1], a[2], a[3], a[4], causal=True)
-    return time.perf_counter() - t0
-
-
-def cpu_baseline():
-    sec = cpu_unit_seconds()
-    # one unit = one head of one sequence; a token needs all H heads
+    sec = time.perf_counter() - t0
     return {"value": N / (sec * H), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"one (batch, head) unit: seq {N}, dim_head {D}, fp32 numpy fwd+bwd, {sec:.2f} s"}
+            "sample": f"one (batch, head) unit, numpy port, {sec:.2f} s ({why})"}
+
+
+def triton_reference(args):
+    """The reference's own Triton kernel (flash_poly_attention,
+    poly_attention/flash_poly_attention.py:448-456) on the config-2 workload,
+    forward + backward, timed on this GPU. Run in a child process so that any
+    failure of the reference's JIT path cannot affect this process."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--workload", "triton_ref", "--steps", str(args.steps),
+           "--warmup", str(args.warmup)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "the Triton reference did not finish within 900 s"}
+    for ln in reversed(r.stdout.splitlines()):
+        if ln.startswith("{"):
+            return json.loads(ln)
+    tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+    return {"unavailable": f"child exited {r.returncode}: {tail[0][:300]}"}
+
+
+def run_triton_ref(args):
+    import torch
+    try:
+        _reference_package()
+        from poly_attention.flash_poly_attention import flash_poly_attention
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"import failed: {type(exc).__name__}: {exc}"}
+    dev = torch.device("cuda", 0)
+    q1, q2, q3, v3, do = make_inputs(dev, 1234, B)
+    ts = [x.requires_grad_(True) for x in (q1, q2, q3, v3)]
+
+    def step():
+        for t in ts:
+            t.grad = None
+        out = flash_poly_attention(*ts, is_causal=True)
+        out.backward(do)
+
+    t0 = time.perf_counter()
+    step()                      # autotune + JIT
+    torch.cuda.synchronize()
+    jit_s = time.perf_counter() - t0
+    for _ in range(args.warmup):
+        step()
+    ms, clk = timed_region(step, args.steps, dev, 1, 0)
+    _, burst, _, kind = peaks()
+    tf = 6 * pass_fwd_flop(B) / (ms * 1e-3) / 1e12
+    return {"impl": "reference Triton kernel (flash_poly_attention) on this GPU", "value": B * N / (ms * 1e-3),
+            "unit": "tokens/s", "ms_per_step": ms, "tflops": tf, "frac": tf / burst,
+            "peak_kind": f"{kind} bf16 burst", "first_call_s": jit_s, "clocks": clk,
+            "config": {"workload": "order-2 causal poly-attention core fwd+bwd (config 2)", "batch": B,
+                       "heads": H, "seq_len": N, "dim_head": D}}
 
 
 def run_reference(args, rank):
+    """--impl reference: the reference's torch CPU path, all host threads,
+    fp32, forward + backward of one sequence x hs heads per step (hs chosen
+    from a one-head calibration so the whole run stays within a few minutes)."""
     if rank != 0:
         return None
+    import torch
+    torch.set_num_threads(os.cpu_count())
+    common = {"metric": METRIC, "impl": "reference", "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+              "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+              "dtype": "f32", "data": "synthetic N(0,1), seeded",
+              "config": {"workload": "order-2 causal poly-attention core fwd+bwd (config 2)", "global_batch": B,
+                         "heads": H, "seq_len": N, "dim_head": D, "parallelism": "cpu"}}
+    try:
+        refmod = _reference_package()
+    except Exception as exc:  # noqa: BLE001
+        port = cpu_baseline_port(str(exc))
+        v = port["value"]
+        return {**common, "value": v, "cpu_baseline": port,
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    g = torch.Generator().manual_seed(1234)
+
+    def inputs(hs):
+        return [torch.randn(1, hs, N, D, generator=g) for _ in range(5)]
+
+    t0 = time.perf_counter()
+    reference_cpu_step(refmod, inputs(1))
+    one = time.perf_counter() - t0
+    hs = int(max(1, min(H, 200.0 / (max(one, 1e-3) * (args.steps + args.warmup)))))
+    ins = inputs(hs)
     for _ in range(args.warmup):
-        cpu_unit_seconds()
-    sec = statistics.median(cpu_unit_seconds() for _ in range(args.steps))
-    v = N / (sec * H)
-    return {
-        "metric": METRIC, "impl": "reference", "value": v, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
-        "config": {"workload": "order-2 causal poly-attention core fwd+bwd (config 2)", "global_batch": B,
-                   "heads": H, "seq_len": N, "dim_head": D, "parallelism": "cpu"},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": "one (batch, head) unit per step, fp32 numpy restatement of the reference"},
-        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
+        reference_cpu_step(refmod, ins)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        reference_cpu_step(refmod, ins)
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    v = N / (sec * H / hs)          # a token needs all 16 heads
+    sample = (f"one sequence x {hs} of 16 heads per step, seq {N}, fp32 torch CPU fwd+bwd of "
+              f"reference_poly_attention (unmodified package in baseline/_ref)")
+    return {**common, "value": v, "ms_per_step": sec * 1e3,
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
@@ -515,12 +719,14 @@ def main():
     ap.add_argument("--batch", type=int, default=B, help="per-GPU batch (smaller for profiling captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-triton", action="store_true", help="skip the reference Triton kernel leg")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 1 / 3 / 4-prefill / 5 legs")
     ap.add_argument("--e2e-chunk", type=int, default=1, help="batch elements per streamed chunk (e2e leg)")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
     ap.add_argument("--decode-batch", type=int, default=32, help="decode leg batch (config 4: 32)")
     ap.add_argument("--decode-cache", type=int, default=2048, help="decode leg prefilled cache length (config 4: 2048)")
-    ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4", "decode"], default="train",
-                    help="train: config 2 fwd+bwd (the headline); longctx: config 5 key-split forward")
+    ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4", "decode", "triton_ref"],
+                    default="train", help="train: everything (the default line); the others run one leg alone")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -528,20 +734,23 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         res = run_reference(args, rank)
+    elif args.workload == "triton_ref":
+        res = run_triton_ref(args) if rank == 0 else None
     else:
+        import torch
         if world > 1:
-            import torch
             import torch.distributed as dist
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
         if args.workload == "longctx":
             res = run_longctx(args, rank, world, local_rank)
+            res = res if rank == 0 else None
         elif args.workload == "decode":
-            import torch
-            res = run_decode(args, torch.device("cuda", local_rank)) if rank == 0 else None
+            res = run_decode(args, dev) if rank == 0 else None
         elif args.workload in ("config1", "vit", "prefill4"):
-            import torch
-            res = run_module_configs(args, torch.device("cuda", local_rank)) if rank == 0 else None
+            res = run_module_config(args.workload, args, dev, local_rank) if rank == 0 else None
         else:
             res = run_ours(args, rank, world, local_rank)
         if world > 1:

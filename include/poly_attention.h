@@ -233,8 +233,10 @@ POLY_API int poly_head_rmsnorm(const PolyHeadNorm* norms, int n, void* stream);
  * allocator has fully planned). Scratch comes from an 8 MiB array built into
  * the library (held per GPU until exit); larger problems get POLY_EINVAL.
  * All calls on a device share that array: calls overlapping on the GPU race.
- * The first call on a device resolves the array's address; make it before
- * any stream capture. args->workspace is ignored.
+ * Every call outside stream capture resolves the array's address afresh
+ * (a device reset leaves no stale address); a call during capture reuses the
+ * last one, so make the first call on a device before any stream capture.
+ * args->workspace is ignored.
  */
 POLY_API int poly_pass_bwd_noalloc(const PolyPassBwdArgs* args, void* stream);
 POLY_API size_t poly_noalloc_scratch_bytes(void);
@@ -254,10 +256,20 @@ POLY_API const char* poly_last_error(void);
 POLY_API unsigned long long poly_launch_count(void);
 
 /* Device error word of the current device (synchronous read): non-zero if a
- * kernel's bounded wait gave up (1 = timeout) since the last reset. The
- * kernel that gave up freed its resources and returned; its outputs are
- * undefined. reset != 0 clears the word. */
+ * kernel's bounded wait gave up since the last reset: 1 | site << 8, the
+ * first give-up wins. The launch that gave up freed its resources and
+ * returned; the outputs of that call are undefined. Other CTAs of the same
+ * launch give up at once; later launches run normally whether or not the
+ * word has been reset. reset != 0 clears the word. */
 POLY_API int poly_device_error(int* out, int reset);
+
+/* Diagnostics, no counterpart in the reference: launches one CTA that holds
+ * TMEM and waits on a barrier nothing arrives on, with a wait limit of
+ * limit_ns (0 < limit_ns <= 1e9), so the bounded-wait give-up path runs:
+ * *result (device int) becomes 2 once the wait gave up and the CTA freed its
+ * TMEM and returned (1 if the wait wrongly succeeded); the device error word
+ * then reads 1 | 99 << 8. */
+POLY_API int poly_selftest_wait_timeout(unsigned long long limit_ns, int* result, void* stream);
 
 /* ABI checks for bindings: POLY_ABI_VERSION and the struct sizes. */
 POLY_API int poly_abi_version(void);

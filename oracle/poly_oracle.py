@@ -72,7 +72,7 @@ def _scores(ql, qr, scale, softclamp_value):
     poly_attention/poly_attention.py:63-66,91-94 ; n_poly_attention.py:237-240
     Returns (scores, tanh_or_None) so the backward can reuse tanh.
     """
-    s = np.einsum("bhid,bhjd->bhij", ql, qr) * ql.dtype.type(scale)
+    s = np.matmul(ql, np.swapaxes(qr, -1, -2)) * ql.dtype.type(scale)
     t = None
     if softclamp_value is not None:
         t = np.tanh(s / s.dtype.type(softclamp_value))
@@ -119,7 +119,7 @@ def pass_fwd(q, k, v, *, scale=None, causal=False, softclamp_value=None,
             s = s + bias[..., None, :].astype(s.dtype)
     lse = _logsumexp(s)
     p = _softmax(s)
-    out = np.einsum("bhij,bhjd->bhid", p, v)
+    out = np.matmul(p, v)
     return out, lse
 
 
@@ -174,8 +174,8 @@ def _pass_bwd(q, k, v, dout, *, scale, causal, softclamp_value, key_mask,
         with np.errstate(over="ignore"):
             s = s + bias[..., None, :].astype(s.dtype)
     p = _softmax(s)
-    dp = np.einsum("bhid,bhjd->bhij", dout, v)
-    dv = np.einsum("bhij,bhid->bhjd", p, dout)
+    dp = np.matmul(dout, np.swapaxes(v, -1, -2))
+    dv = np.matmul(np.swapaxes(p, -1, -2), dout)
     ds = p * (dp - np.sum(p * dp, axis=-1, keepdims=True))
     if dlse is not None:
         ds = ds + p * dlse[..., None]
@@ -183,8 +183,8 @@ def _pass_bwd(q, k, v, dout, *, scale, causal, softclamp_value, key_mask,
     dz = np.where(keep, ds, 0)
     if t is not None:
         dz = dz * (1 - t * t)
-    dq = np.einsum("bhij,bhjd->bhid", dz, k) * scale
-    dk = np.einsum("bhij,bhid->bhjd", dz, q) * scale
+    dq = np.matmul(dz, k) * scale
+    dk = np.matmul(np.swapaxes(dz, -1, -2), q) * scale
     return dq, dk, dv, dbias
 
 
@@ -252,7 +252,7 @@ def npoly_chain_fwd(q_left, q_right, vs_full, *, causal=False,
 
     for k in range(order - 1, 1, -1):
         lse_step = _logsumexp(cur)
-        msg_step = np.einsum("bhij,bhjd->bhid", _softmax(cur), out)
+        msg_step = np.matmul(_softmax(cur), out)
         idx = (order - 1) - k
         lse_full = cat(c_lses[idx], lse_step, -1)
         msg_full = cat(c_msgs[idx], msg_step, -2)
@@ -263,7 +263,7 @@ def npoly_chain_fwd(q_left, q_right, vs_full, *, causal=False,
             cur = lse_full[..., None, :] + scores[k - 1]
 
     lse1_step = _logsumexp(cur)
-    msg1_step = np.einsum("bhij,bhjd->bhid", _softmax(cur), out)
+    msg1_step = np.matmul(_softmax(cur), out)
     idx = order - 2
     lse1_full = cat(c_lses[idx], lse1_step, -1)
     msg1_full = cat(c_msgs[idx], msg1_step, -2)
@@ -271,7 +271,7 @@ def npoly_chain_fwd(q_left, q_right, vs_full, *, causal=False,
     new_lses.append(lse1_full)
     with np.errstate(over="ignore"):
         s12 = lse1_full[..., None, :] + scores[0]
-    out = np.einsum("bhij,bhjd->bhid", _softmax(s12), msg1_full)
+    out = np.matmul(_softmax(s12), msg1_full)
     return out, new_lses, new_msgs
 
 

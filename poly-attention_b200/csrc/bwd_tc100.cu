@@ -31,7 +31,7 @@
 namespace poly {
 
 // Device error word of this file's kernels (see read_device_error_bwd).
-static __device__ int g_poly_device_error = 0;
+static __device__ int g_poly_device_error[2] = {0, 0};
 
 int read_device_error_bwd(int* out, bool reset) {
   int rc = cuda_status(cudaMemcpyFromSymbol(out, g_poly_device_error, sizeof(int)), "read device error word");
@@ -50,6 +50,7 @@ constexpr int BK = 128;   // keys per CTA
 constexpr int BQ = 128;   // queries per tile
 constexpr int kThreads = 384;
 constexpr int kHeadGroup = 8;
+constexpr int kSelftestSite = 99;   // error-record site of wait_selftest_kernel
 
 struct BwdLayout {
   static constexpr int kTile = 128 * D * 2;  // 16 KB: one [128][64] 16-bit tile
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = bars + 13;
   uint32_t* tmem_slot = (uint32_t*)(smem + L::kMisc);
   volatile int* abort_flag = (volatile int*)(smem + L::kMisc + 4);
-  int* err = &g_poly_device_error;
+  int* err = g_poly_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // 1-D grid over (head group of kHeadGroup (batch, kv head)s, key tile,
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(mma_done, 1);
     mbar_init(dkv_done, 1);
     mbar_init(drain, 1);
-    *abort_flag = 0;
+    tc::abort_init(abort_flag, err);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, L::kTmemCols);
@@ -465,8 +466,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-#include "bwd2_body.cuh"
-
 // delta_i = dout_i . out_i - dlse_i and nlse2_i = -lse_i * log2(e), padded to
 // nq_pad rows per (batch, head) with (delta 0, nlse2 -inf) so padded queries
 // get p = 0. Eight lanes per row, 16-byte loads.
@@ -566,30 +565,14 @@ BwdWs bwd_ws(const PolyPassBwdArgs& a) {
   return w;
 }
 
-// POLY_BWD_TWO_TILE=1 selects the two-tile pipelined kernel (bwd2_body.cuh):
-// correct, but slower than pass_bwd_tc_kernel at config 2 (1.50 vs 1.37 ms
-// per pass), so it is opt-in.
-bool bwd_two_tile() {
-  static const bool v = [] {
-    const char* e = getenv("POLY_BWD_TWO_TILE");
-    return e && e[0] == '1';
-  }();
-  return v;
-}
-
 template <typename T, bool SOFTCLAMP, bool HAS_BIAS, bool DB>
 int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   using L = BwdLayout;
-  constexpr bool kTwo = !SOFTCLAMP;   // the two-tile kernel has no softclamp path
-  const bool two = kTwo && bwd_two_tile();
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS, DB>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (attr_err == cudaSuccess && kTwo)
-      attr_err = cudaFuncSetAttribute(pass_bwd_tc2_kernel<T, HAS_BIAS, DB>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, Bwd2Layout::kAlloc);
   });
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "cudaFuncSetAttribute(bwd tc)");
   const PolyPassArgs& f = a.fwd;
@@ -634,10 +617,7 @@ int launch_bwd_t(const PolyPassBwdArgs& a, cudaStream_t s) {
   p.dbias_stride[1] = a.dbias_stride[1];
   p.k_tiles = (f.seq_k + BK - 1) / BK;
   dim3 grid(p.k_tiles * f.batch * f.kv_heads);
-  if (two)
-    pass_bwd_tc2_kernel<T, HAS_BIAS, DB><<<grid, kThreads, Bwd2Layout::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
-  else
-    pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS, DB><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
+  pass_bwd_tc_kernel<T, SOFTCLAMP, HAS_BIAS, DB><<<grid, kThreads, L::kAlloc, s>>>(tq, tdo, tk, tv, tdq, p);
   const int64_t cthreads = (int64_t)f.batch * f.heads * f.seq_q * (D / 8);
   bwd_dq_convert_kernel<T><<<(unsigned)((cthreads + 255) / 256), 256, 0, s>>>(a, w.dq_acc);
   note_launch(3);
@@ -655,7 +635,40 @@ int bwd_dispatch(const PolyPassBwdArgs& a, cudaStream_t s) {
   return bias ? launch_bwd_t<T, false, true, false>(a, s) : launch_bwd_t<T, false, false, false>(a, s);
 }
 
+// Self-test of the bounded waits (poly_selftest_wait_timeout): one CTA holds
+// TMEM like the pass kernels do, waits on an mbarrier that nothing arrives on,
+// with a limit of limit_ns, and must give up through the same path as a real
+// timeout: error record of this file, CTA abort flag, TMEM freed, return.
+// result: 1 if the wait (wrongly) succeeded, 2 if it gave up.
+__global__ void __launch_bounds__(64, 1) wait_selftest_kernel(uint64_t limit_ns, int* result) {
+  __shared__ uint64_t bar;
+  __shared__ uint32_t slot;
+  __shared__ int abort_state[2];
+  int* err = g_poly_device_error;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_init(abort_state, err);
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 32) tmem_alloc(&slot, 32);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const bool ok = mbar_wait_warp(&bar, 0, abort_state, err, kSelftestSite, limit_ns);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc(slot, 32);
+  if (threadIdx.x == 0) *result = ok ? 1 : 2;
+}
+
 }  // namespace
+
+int selftest_wait_timeout(uint64_t limit_ns, int* result, cudaStream_t s) {
+  wait_selftest_kernel<<<1, 64, 0, s>>>(limit_ns, result);
+  note_launch(1);
+  return cuda_status(cudaGetLastError(), "wait_selftest_kernel launch");
+}
 
 bool pass_bwd_tc_eligible(const PolyPassBwdArgs& a) {
   const PolyPassArgs& f = a.fwd;

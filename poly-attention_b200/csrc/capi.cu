@@ -21,11 +21,6 @@ static int fail(int code, const std::string& msg) {
   return code;
 }
 
-static bool force_simt() {
-  const char* e = std::getenv("POLY_FORCE_SIMT");
-  return e && e[0] == '1';
-}
-
 static int check_pass(const PolyPassArgs* a) {
   if (!a) return fail(POLY_EINVAL, "null args");
   if (a->batch <= 0 || a->heads <= 0 || a->kv_heads <= 0 || a->seq_q < 0 || a->seq_k <= 0 || a->head_dim <= 0)
@@ -42,7 +37,6 @@ static int check_pass(const PolyPassArgs* a) {
 enum class FwdKind { kSimt, kTc, kDecode, kSmall, kF32 };
 
 static FwdKind choose_fwd(const PolyPassArgs& a) {
-  if (force_simt()) return FwdKind::kSimt;
   if (pass_decode_eligible(a)) return FwdKind::kDecode;
   if (pass_small_eligible(a)) return FwdKind::kSmall;
   if (pass_f32_eligible(a)) return FwdKind::kF32;
@@ -50,7 +44,7 @@ static FwdKind choose_fwd(const PolyPassArgs& a) {
   return FwdKind::kSimt;
 }
 
-static bool use_bwd_tc(const PolyPassBwdArgs& a) { return !force_simt() && pass_bwd_tc_eligible(a); }
+static bool use_bwd_tc(const PolyPassBwdArgs& a) { return pass_bwd_tc_eligible(a); }
 
 static size_t simt_bwd_workspace(const PolyPassBwdArgs& a) {
   return (size_t)a.fwd.batch * a.fwd.heads * (size_t)a.fwd.seq_q * (sizeof(float) + sizeof(int));
@@ -74,6 +68,11 @@ int poly_device_error(int* out, int reset) {
   if (!rc) rc = read_device_error_dec(&d, reset != 0);
   *out = a ? a : (c ? c : (b ? b : d));
   return rc;
+}
+int poly_selftest_wait_timeout(unsigned long long limit_ns, int* result, void* stream) {
+  if (!result) return fail(POLY_EINVAL, "null result");
+  if (limit_ns == 0 || limit_ns > 1000000000ull) return fail(POLY_EINVAL, "limit_ns must be in (0, 1e9]");
+  return selftest_wait_timeout(limit_ns, result, (cudaStream_t)stream);
 }
 int poly_abi_version(void) { return POLY_ABI_VERSION; }
 size_t poly_sizeof_pass_args(void) { return sizeof(PolyPassArgs); }

@@ -82,7 +82,7 @@ __host__ __device__ constexpr int smem_bytes() {   // + bias, barriers, flag, al
   return ring_bytes<D, R, NARR>() + num_stages<D, NARR>() * (kTile * 4 + 16) + 16 + 1024;
 }
 
-static __device__ int g_decode_error = 0;
+static __device__ int g_decode_error[2] = {0, 0};
 
 __device__ __forceinline__ void cp_async4(uint32_t sa, const void* gmem, bool valid) {
   const int n = valid ? 4 : 0;   // zero-fill past the end
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
   uint64_t* full = reinterpret_cast<uint64_t*>(sbias + NST * kTile);
   uint64_t* empty = full + NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
-  int* err = &g_decode_error;
+  int* err = g_decode_error;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
       tc::mbar_init(&full[s], HAS_BIAS ? 33 : 1);   // producer lane 0 (+ tx), + 32 bias lanes
       tc::mbar_init(&empty[s], kWarps);
     }
-    *abort_flag = 0;
+    tc::abort_init(abort_flag, err);
     tc::fence_barrier_init();
   }
   __syncthreads();
@@ -528,16 +528,11 @@ struct DecodeGeom {
 // Splits per group: the most (<= kMaxSplits) that still fit every CTA of the
 // grid into one wave (`slots` = resident CTAs per SM x SMs), so that each CTA
 // streams one long key range and pays its pipeline ramp-up and merge once;
-// at least one 64-key tile per split. POLY_DECODE_SPLITS overrides (tuning).
+// at least one 64-key tile per split.
 DecodeGeom geometry(const PolyPassArgs& a, int slots) {
   const int groups = a.batch * a.kv_heads;
   const int ntiles = (a.seq_k + kTile - 1) / kTile;
   int splits = max(1, min(kMaxSplits, slots / max(groups, 1)));
-  static const int forced = [] {
-    const char* e = getenv("POLY_DECODE_SPLITS");
-    return e ? atoi(e) : 0;
-  }();
-  if (forced > 0) splits = min(forced, kMaxSplits);
   splits = max(1, min(splits, ntiles));
   DecodeGeom gm;
   gm.kps = max(kTile, ((a.seq_k + splits - 1) / splits + kTile - 1) / kTile * kTile);
@@ -574,11 +569,6 @@ int global_splits(const PolyPassArgs& a) {
   const int groups = max(1, a.batch * a.kv_heads);
   const int ntiles = (a.seq_k + kTile - 1) / kTile;
   const int target = 2 * sm_count();
-  static const bool off = [] {                // POLY_DECODE_GLOBAL=0: cluster path only (tuning)
-    const char* e = getenv("POLY_DECODE_GLOBAL");
-    return e && e[0] == '0';
-  }();
-  if (off) return 0;
   const int want = min(kMaxGlobalSplits, min(ntiles / kMinGlobalTiles, target / groups));
   if (want <= kMaxSplits) return 0;
   const int kps = ((a.seq_k + want - 1) / want + kTile - 1) / kTile * kTile;

@@ -22,7 +22,7 @@
 
 namespace poly {
 
-static __device__ int g_poly_device_error = 0;
+static __device__ int g_poly_device_error[2] = {0, 0};
 
 int read_device_error_fwd2(int* out, bool reset) {
   int rc = cuda_status(cudaMemcpyFromSymbol(out, g_poly_device_error, sizeof(int)), "read device error word");
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = bars + 9 + 3 * S;
   uint32_t* tmem_slot = (uint32_t*)(smem + L2::kMisc);
   volatile int* abort_flag = (volatile int*)(smem + L2::kMisc + 4);
-  int* err = &g_poly_device_error;
+  int* err = g_poly_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // grid: x = (batch, head), y = query-tile pair, heaviest (most key tiles)
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_done[x], 1);
     }
     mbar_init(drain, 1);
-    *abort_flag = 0;
+    tc::abort_init(abort_flag, err);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, L2::kTmemCols);

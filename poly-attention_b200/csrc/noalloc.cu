@@ -19,9 +19,12 @@
 //   * the array keeps whatever the previous call left in it; the kernels
 //     clear or fully overwrite every part they read (the dQ accumulator is
 //     zeroed on the stream first), so no stale state leaks into results;
-//   * the first call on each device resolves the array's device address
-//     (cudaGetSymbolAddress, with that device current); make that first call
-//     before any stream capture begins.
+//   * every call made outside stream capture resolves the array's device
+//     address again (cudaGetSymbolAddress, with the call's device current),
+//     so a device reset or a re-created primary context never leaves a stale
+//     address behind; a call made during stream capture reuses the address
+//     the device's last uncaptured call resolved, so the first call on each
+//     device must come before any stream capture begins.
 #include <mutex>
 #include <string>
 
@@ -41,7 +44,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
 
-int scratch_for_current_device(void** out) {
+int scratch_for_current_device(cudaStream_t stream, void** out) {
   int dev = -1;
   int rc = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
   if (rc) return rc;
@@ -49,12 +52,18 @@ int scratch_for_current_device(void** out) {
     set_error("device index out of range for the no-allocation scratch table");
     return POLY_EUNSUPPORTED;
   }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  rc = cuda_status(cudaStreamIsCapturing(stream, &cap), "cudaStreamIsCapturing");
+  if (rc) return rc;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  if (cap == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)");
     if (rc) return rc;
     g_noalloc_ptr[dev] = p;
+  } else if (!g_noalloc_ptr[dev]) {
+    set_error("poly_pass_bwd_noalloc: the first call on a device must come before stream capture");
+    return POLY_EINVAL;
   }
   *out = g_noalloc_ptr[dev];
   return POLY_OK;
@@ -78,7 +87,7 @@ extern "C" POLY_API int poly_pass_bwd_noalloc(const PolyPassBwdArgs* args, void*
     return POLY_EINVAL;
   }
   void* scratch = nullptr;
-  const int rc = poly::scratch_for_current_device(&scratch);
+  const int rc = poly::scratch_for_current_device((cudaStream_t)stream, &scratch);
   if (rc) return rc;
   PolyPassBwdArgs a = *args;
   a.workspace = scratch;

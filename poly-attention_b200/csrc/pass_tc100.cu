@@ -31,7 +31,7 @@ namespace poly {
 // Device error word of this file's kernels: set by bounded waits that gave up.
 // (Without relocatable device code every .cu file has its own; the host
 // combines them in poly_device_error.)
-static __device__ int g_poly_device_error = 0;
+static __device__ int g_poly_device_error[2] = {0, 0};
 
 int read_device_error_fwd(int* out, bool reset) {
   int rc = cuda_status(cudaMemcpyFromSymbol(out, g_poly_device_error, sizeof(int)), "read device error word");
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* bias_ready = bars + 6 + 3 * S;   // [2]
   uint32_t* tmem_slot = (uint32_t*)(smem + L::kMisc);
   volatile int* abort_flag = (volatile int*)(smem + L::kMisc + 4);
-  int* err = &g_poly_device_error;
+  int* err = g_poly_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // grid: x = (batch, head), y = query tile, heaviest first (longest-first dispatch)
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     mbar_init(drain, 1);
     mbar_init(&bias_ready[0], 128);
     mbar_init(&bias_ready[1], 128);
-    *abort_flag = 0;
+    tc::abort_init(abort_flag, err);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, L::kTmemCols);
@@ -481,8 +481,7 @@ bool pass_fwd_tc_eligible(const PolyPassArgs& a) {
 size_t pass_fwd_tc_workspace(const PolyPassArgs&) { return 0; }
 
 int launch_pass_fwd_tc(const PolyPassArgs& a, cudaStream_t s) {
-  const char* one = std::getenv("POLY_FWD_ONE_TILE");
-  if (!(one && one[0] == '1') && pass_fwd_tc2_eligible(a)) return launch_pass_fwd_tc2(a, s);
+  if (pass_fwd_tc2_eligible(a)) return launch_pass_fwd_tc2(a, s);
   if (a.dtype == POLY_BF16)
     return a.head_dim == 64 ? fwd_bias<64, __nv_bfloat16>(a, s) : fwd_bias<128, __nv_bfloat16>(a, s);
   return a.head_dim == 64 ? fwd_bias<64, __half>(a, s) : fwd_bias<128, __half>(a, s);

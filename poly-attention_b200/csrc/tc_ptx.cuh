@@ -10,11 +10,15 @@ namespace poly {
 namespace tc {
 
 // Every spin-wait below gives up after kWaitNs nanoseconds of wall time
-// (%globaltimer). A wait that gives up records where it was in the device
-// error word (kErrTimeout | site << 8, first writer wins) and raises the
-// CTA-local abort flag; every other wait in the grid that sees a non-zero
-// error word gives up at once. Each role then leaves its loop, the CTA frees
-// its TMEM and returns, and the host reads the word (poly_device_error).
+// (%globaltimer). The error record of a kernel file is int[2]: err[0] = the
+// first give-up's code (kErrTimeout | site << 8, first writer wins, cleared by
+// poly_device_error(reset)), err[1] = how many waits ever gave up (monotonic,
+// never cleared). Each CTA keeps abort[0] (its own abort flag) and abort[1]
+// (err[1] as it was when the CTA started, see abort_init). A wait gives up at
+// once when its CTA has aborted or when err[1] moved past abort[1], i.e. a
+// CTA that started no earlier than this one gave up: the failure of one
+// launch stops the rest of that launch fast, but a later launch is not
+// poisoned by an old, unreset error word.
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
 constexpr int kErrTimeout = 1;
 
@@ -58,23 +62,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Start-of-CTA state for the bounded waits (one thread, before the CTA's
+// first barrier).
+__device__ __forceinline__ void abort_init(volatile int* abort, const int* err) {
+  abort[0] = 0;
+  abort[1] = err ? *(const volatile int*)(err + 1) : 0;
+}
+
 // Bounded wait. Returns false (and raises *abort) on timeout, or if another
 // role of this CTA or any CTA of the grid already gave up. `site` names the
 // barrier for the error word.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
-                                          int site = 0) {
+                                          int site = 0, uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
-      if (*abort || (err && *(volatile int*)err)) {
+      if (*abort || (err && *(const volatile int*)(err + 1) != abort[1])) {
         *abort = 1;
         return false;
       }
-      if (globaltimer() - t0 > kWaitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort = 1;
-        if (err) atomicCAS(err, 0, kErrTimeout | (site << 8));
+        if (err) {
+          atomicCAS(err, 0, kErrTimeout | (site << 8));
+          atomicAdd(err + 1, 1);
+        }
         return false;
       }
     }
@@ -84,8 +98,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Same, with a warp-uniform result: roles whose warps then run
 // warp-collective tcgen05.ld / st must never split a warp on a wait.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
-                                               int site = 0) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, err, site));
+                                               int site = 0, uint64_t limit_ns = kWaitNs) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, err, site, limit_ns));
 }
 
 // ---------------------------------------------------------------- TMA

@@ -94,6 +94,7 @@ EXPORTS = {
     "poly_last_error": (ctypes.c_char_p, []),
     "poly_launch_count": (ctypes.c_ulonglong, []),
     "poly_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    "poly_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_ulonglong, c_vp, c_vp]),
     "poly_abi_version": (ctypes.c_int, []),
     "poly_sizeof_pass_args": (c_sz, []),
     "poly_sizeof_pass_bwd_args": (c_sz, []),

@@ -23,6 +23,12 @@ Cases (all fp32, CPU, seeded):
 * ``modn_*``     ``NPolyAttention`` order 3 and 4 forward (n_poly_attention.py),
   with a stepwise-cache run, plus chain-level gradients captured with hooks
   on the q-norm outputs, the kv projections and the output projection input.
+* ``vit_*``      ``PolyViT`` forward, small; ``vit_full``: the full config-3
+  model (dim 1024, depth 6) on 2 images, outputs only (weights and images
+  come from seeds, tests/golden/seeded.py).
+
+``python tests/golden/make_golden.py [case ...]`` regenerates only the named
+case groups (ref_fn, mod2, modn, vit, vit_full).
 """
 from __future__ import annotations
 
@@ -37,6 +43,7 @@ REF = os.environ.get("POLY_REFERENCE")
 if not REF or not os.path.isdir(os.path.join(REF, "poly_attention")):
     sys.exit("set POLY_REFERENCE to a checkout of lucidrains/poly-attention (the directory holding poly_attention/)")
 sys.path.insert(0, os.path.join(HERE, "shims"))
+sys.path.insert(0, HERE)
 sys.path.insert(0, REF)
 
 from poly_attention.poly_attention import reference_poly_attention, Order2PolyAttention  # noqa: E402
@@ -236,9 +243,24 @@ def vit_cases():
         save(f"vit_o{order}", img=np32(img), y=np32(y), **{f"p:{k}": v for k, v in state_np(m).items()})
 
 
+def vit_full_case():
+    # full-size PolyViT of BASELINE config 3 (poly_attention/poly_vit.py:65-101)
+    # on 2 images: only the outputs are committed; weights and images are
+    # rebuilt from seeds (tests/golden/seeded.py)
+    from seeded import VIT_FULL, VIT_FULL_IMG_SEED, VIT_FULL_SEED, seeded_images, seeded_state_dict
+    m = PolyViT(**VIT_FULL)
+    sd = seeded_state_dict([(k, v.shape) for k, v in m.state_dict().items()], VIT_FULL_SEED)
+    m.load_state_dict(sd)
+    img = seeded_images(2, VIT_FULL_IMG_SEED)
+    with torch.no_grad():
+        y = m(img)
+    save("vit_full", y=np32(y), img_checksum=np.float64(img.double().sum().item()),
+         weight_checksum=np.float64(sum(v.double().abs().sum().item() for v in sd.values())))
+
+
+CASES = {"ref_fn": ref_fn_cases, "mod2": mod2_cases, "modn": modn_cases, "vit": vit_cases, "vit_full": vit_full_case}
+
 if __name__ == "__main__":
     torch.set_num_threads(4)
-    ref_fn_cases()
-    mod2_cases()
-    modn_cases()
-    vit_cases()
+    for name in (sys.argv[1:] or list(CASES)):
+        CASES[name]()

@@ -1,0 +1,134 @@
+"""Parity at the full BASELINE shapes that bench.py times.
+
+The small-case parity tests pin every kernel and code path; these run the
+CUDA path at the benchmarked sizes and compare against the oracle (or, where
+the oracle would need an n x n tensor of every head at once, a chunked fp32
+restatement in the test itself) on sampled units:
+
+* config 2: order-2 causal fwd + bwd, b8 h16 n4096 d64 bf16, 3 sampled
+  (batch, head) units of out, dq1, dq2, dq3, dv3;
+* config 4 prefill: NPolyAttention(dim=2048, order=3, heads=16, kv_heads=4,
+  dim_head=128, causal=True) on x [32, 2048, 2048] bf16, one sequence;
+* config 5: the long-context forward at n = 32768 (keys split as on N GPUs,
+  here one), 2 heads x 256 sampled query rows;
+* config 3: the full PolyViT (dim 1024, depth 6) against the reference's own
+  outputs (tests/golden/vit_full.npz), fp32 and bf16.
+
+Tolerances: bf16 against fp32 within max-abs 2e-2 / rel 1e-2; fp32 within 1e-4.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import poly_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+BF16_ATOL, BF16_RTOL = 2e-2, 1e-2
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def test_config2_fullsize_sampled_units():
+    import poly_attention_b200 as P
+    b, h, n, d = 8, 16, 4096, 64
+    g = torch.Generator(device="cuda").manual_seed(2024)
+    ts = [torch.randn(b, h, n, d, device="cuda", dtype=torch.bfloat16, generator=g).requires_grad_(True)
+          for _ in range(4)]
+    do = torch.randn(b, h, n, d, device="cuda", dtype=torch.bfloat16, generator=g)
+    out, _, _ = P.poly_attention_order2(*ts, causal=True)
+    out.backward(do)
+    torch.cuda.synchronize()
+    for bi, hi in ((0, 0), (3, 7), (7, 15)):
+        a = [host(t[bi:bi + 1, hi:hi + 1]) for t in ts]
+        g_do = host(do[bi:bi + 1, hi:hi + 1])
+        ref, _, _ = O.order2_fwd(a[0], a[1], a[1], a[2], a[3], causal=True)
+        gr = O.order2_bwd(a[0], a[1], a[1], a[2], a[3], g_do, causal=True)
+        want = {"out": ref, "dq1": gr[0], "dq2": gr[1] + gr[2], "dq3": gr[3], "dv3": gr[4]}
+        got = {"out": out, "dq1": ts[0].grad, "dq2": ts[1].grad, "dq3": ts[2].grad, "dv3": ts[3].grad}
+        for k, w in want.items():
+            np.testing.assert_allclose(host(got[k][bi:bi + 1, hi:hi + 1]), w, atol=BF16_ATOL, rtol=BF16_RTOL,
+                                       err_msg=f"{k} at (b={bi}, h={hi})")
+
+
+def test_config4_prefill_fullsize_one_sequence():
+    import poly_attention_b200 as P
+    torch.manual_seed(4)
+    m = P.NPolyAttention(dim=2048, order=3, heads=16, kv_heads=4, dim_head=128, causal=True).cuda().to(
+        torch.bfloat16)
+    g = torch.Generator(device="cuda").manual_seed(44)
+    x = torch.randn(32, 2048, 2048, device="cuda", dtype=torch.bfloat16, generator=g)
+    with torch.no_grad():
+        y = m(x)
+    torch.cuda.synchronize()
+    p = {k: host(v) for k, v in m.state_dict().items()}
+    for bi in (0, 31):
+        want = O.npoly_module_fwd(p, host(x[bi:bi + 1]), order=3, heads=16, kv_heads=4, causal=True)
+        np.testing.assert_allclose(host(y[bi:bi + 1]), want, atol=BF16_ATOL, rtol=BF16_RTOL, err_msg=f"seq {bi}")
+
+
+def _order2_rows_fp32(q1, q2, q3, v3, rows, chunk=2048):
+    """Causal order-2 output of the given query rows for one (batch, head),
+    fp32 on the CPU, without holding an n x n matrix: pass 1
+    (poly_attention/poly_attention.py:63-82) for every key row in chunks of
+    queries, then pass 2 (:91-114) for the sampled rows."""
+    n, d = q1.shape
+    scale = d ** -0.5
+    lse23 = torch.empty(n)
+    msg = torch.empty(n, d)
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        sim = (q2[s:e] @ q3[:e].T) * scale
+        i = torch.arange(s, e)[:, None]
+        sim = sim.masked_fill(torch.arange(e)[None, :] > i, -torch.finfo(torch.float32).max)
+        lse23[s:e] = torch.logsumexp(sim, -1)
+        msg[s:e] = torch.softmax(sim, -1) @ v3[:e]
+    sim = (q1[rows] @ q2.T) * scale
+    sim = sim.masked_fill(torch.arange(n)[None, :] > rows[:, None], -torch.finfo(torch.float32).max)
+    sim = sim + lse23[None, :]
+    return torch.softmax(sim, -1) @ msg
+
+
+def test_config5_longctx_sampled_rows():
+    from poly_attention_b200.distributed import context_parallel_order2_fwd, zigzag_shard, zigzag_unshard
+    b, h, n, d = 1, 16, 32768, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ts = [torch.randn(b, h, n, d, device="cuda", dtype=torch.bfloat16, generator=g) for _ in range(4)]
+    out = zigzag_unshard([context_parallel_order2_fwd(*(zigzag_shard(t, 0, 1) for t in ts))], 1)
+    torch.cuda.synchronize()
+    torch.set_num_threads(os.cpu_count())
+    rows = torch.cat([torch.arange(0, 8), torch.randint(8, n, (240,), generator=torch.Generator().manual_seed(0)),
+                      torch.arange(n - 8, n)])
+    for hi in (0, 11):
+        q1, q2, q3, v3 = [t[0, hi].float().cpu() for t in ts]
+        want = _order2_rows_fp32(q1, q2, q3, v3, rows)
+        np.testing.assert_allclose(host(out[0, hi, rows]), want.numpy(), atol=BF16_ATOL, rtol=BF16_RTOL,
+                                   err_msg=f"head {hi}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_config3_polyvit_full(golden, dtype):
+    import poly_attention_b200 as P
+    sys.path.insert(0, os.path.join(HERE, "golden"))
+    from seeded import VIT_FULL, VIT_FULL_IMG_SEED, VIT_FULL_SEED, seeded_images, seeded_state_dict
+    gd = golden("vit_full")
+    m = P.PolyViT(**VIT_FULL)
+    sd = seeded_state_dict([(k, v.shape) for k, v in m.state_dict().items()], VIT_FULL_SEED)
+    assert sum(v.double().abs().sum().item() for v in sd.values()) == pytest.approx(float(gd["weight_checksum"]),
+                                                                                     rel=1e-9)
+    m.load_state_dict(sd)
+    img = seeded_images(2, VIT_FULL_IMG_SEED)
+    assert img.double().sum().item() == pytest.approx(float(gd["img_checksum"]), rel=1e-9)
+    m = m.cuda().to(dtype)
+    with torch.no_grad():
+        y = m(img.cuda().to(dtype))
+    if dtype == torch.float32:
+        np.testing.assert_allclose(host(y), gd["y"], atol=1e-4, rtol=0)
+    else:
+        np.testing.assert_allclose(host(y), gd["y"], atol=BF16_ATOL, rtol=BF16_RTOL)

@@ -68,6 +68,8 @@ def test_noalloc_rejects_oversized_problem():
     g = [torch.empty_like(q) for _ in range(4)]
     db = torch.empty(b, h, n, device="cuda")
     a, keep = _args(q, q, q, out, lse, g[0], g[1], g[2], g[3], db, True)
+    # the rejection must come from the size check, not from a kernel choice with a smaller workspace
+    assert _lib.lib.poly_pass_bwd_workspace_size(ctypes.byref(a)) > _lib.lib.poly_noalloc_scratch_bytes()
     rc = _lib.lib.poly_pass_bwd_noalloc(ctypes.byref(a), None)
     assert rc == _lib.POLY_EINVAL
     assert "scratch" in _lib.lib.poly_last_error().decode()
