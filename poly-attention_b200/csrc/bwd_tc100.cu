@@ -9,7 +9,9 @@
 //   S^T  = K Q_t^T        (M=128 keys, N=128 queries, K=64)   -> TMEM
 //   dP^T = V dO_t^T                                          -> TMEM
 //   two softmax warpgroups (thread = key row j, warpgroup hw takes query
-//   columns [64 hw, 64 hw + 64)):
+//   columns [64 hw, 64 hw + 64)) load their whole slice of S^T and dP^T into
+//   registers and release the two TMEM buffers at once, so S^T / dP^T of
+//   tile t + 1 are computed while they work on tile t:
 //     p = exp2(s*log2e*scale + bias_j - lse2_i), ds = p (dp - delta_i),
 //     dbias_j += ds (a register: the column sum of dS needs no reduction),
 //     P^T -> TMEM (16-bit), dS^T (x softclamp factor) -> 128B-swizzled smem
@@ -56,13 +58,14 @@ struct BwdLayout {
   static constexpr int kTile = 128 * D * 2;  // 16 KB: one [128][64] 16-bit tile
   static constexpr int kK = 0;
   static constexpr int kV = kK + kTile;
-  static constexpr int kQ = kV + kTile;          // 2 stages
-  static constexpr int kDO = kQ + 2 * kTile;     // 2 stages
-  static constexpr int kDST = kDO + 2 * kTile;   // dS^T [128 keys][128 queries], read MN-major by dQ
+  static constexpr int kStages = 3;              // Q / dO / lse / delta stages
+  static constexpr int kQ = kV + kTile;
+  static constexpr int kDO = kQ + kStages * kTile;
+  static constexpr int kDST = kDO + kStages * kTile;  // dS^T [128 keys][128 queries], read MN-major by dQ
   static constexpr int kDQS = kDST + 2 * kTile;  // dQ staging: 2 x [128 rows][32 fp32], swizzled
-  static constexpr int kLse = kDQS + 2 * kTile;  // 2 stages x 128 floats
-  static constexpr int kDel = kLse + 2 * BQ * 4;
-  static constexpr int kDb = kDel + 2 * BQ * 4;   // d-bias partials of warpgroup 1
+  static constexpr int kLse = kDQS + 2 * kTile;  // kStages x 128 floats
+  static constexpr int kDel = kLse + kStages * BQ * 4;
+  static constexpr int kDb = kDel + kStages * BQ * 4;   // d-bias partials of warpgroup 1
   static constexpr int kBar = kDb + BK * 4;
   static constexpr int kNumBars = 16;
   static constexpr int kMisc = kBar + kNumBars * 8;
@@ -175,16 +178,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* sDb = (float*)(smem + L::kDb);
   float dbias_part = 0.f;
   uint64_t* bars = (uint64_t*)(smem + L::kBar);
+  constexpr int QS = L::kStages;
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;     // [2]
-  uint64_t* q_empty = bars + 3;    // [2]
-  uint64_t* sdp_full = bars + 5;
-  uint64_t* p_ready = bars + 6;
-  uint64_t* mma_done = bars + 7;
-  uint64_t* dq_full = bars + 8;    // [2]
-  uint64_t* dq_free = bars + 10;   // [2]
-  uint64_t* dkv_done = bars + 12;
-  uint64_t* drain = bars + 13;
+  uint64_t* q_full = bars + 1;     // [QS]
+  uint64_t* q_empty = bars + 4;    // [QS]
+  uint64_t* sdp_full = bars + 7;   // S^T / dP^T of the tile are in TMEM
+  uint64_t* sdp_free = bars + 8;   // ... and in the softmax threads' registers
+  uint64_t* p_ready = bars + 9;
+  uint64_t* mma_done = bars + 10;
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_free = bars + 12;
+  uint64_t* dkv_done = bars + 13;
+  uint64_t* drain = bars + 14;
   uint32_t* tmem_slot = (uint32_t*)(smem + L::kMisc);
   volatile int* abort_flag = (volatile int*)(smem + L::kMisc + 4);
   int* err = g_poly_device_error;
@@ -212,13 +217,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < QS; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
-      mbar_init(&dq_full[s], 1);
-      mbar_init(&dq_free[s], 128);
     }
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
     mbar_init(sdp_full, 1);
+    mbar_init(sdp_free, 256);
     mbar_init(p_ready, 256);
     mbar_init(mma_done, 1);
     mbar_init(dkv_done, 1);
@@ -240,21 +246,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // dQ of tile t: TMEM -> swizzled fp32 smem tile -> one TMA reduce-add into
   // the accumulator. Run by softmax warpgroup 0 (warps 4-7, all four TMEM lane
-  // quarters) right after it has handed tile t + 1 to the MMA. Returns false
-  // if a wait gave up; the decision is shared by the warpgroup.
+  // quarters) right after it has handed tile t + 1 to the MMA. Its cost is
+  // latency (barriers, shared-memory stores competing with the MMAs' operand
+  // reads, the TMA issue), not volume: splitting it over both warpgroups
+  // measured slower. Returns false if a wait gave up; the decision is shared
+  // by the warpgroup.
   auto stage_dq = [&](int t) -> bool {
     int h, qt;
     tile_of(t, h, qt);
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    if (!named_bar_and(3, 128, mbar_wait_warp(&dq_full[0], t & 1, abort_flag, err, 10))) return false;
+    if (!named_bar_and(3, 128, mbar_wait_warp(dq_full, t & 1, abort_flag, err, 10))) return false;
     tc_fence_after();
     uint32_t a[32], c2[32];
     tmem_ld32(tmem + lane_base + L::kDQ, a);
     tmem_ld32(tmem + lane_base + L::kDQ + 32, c2);
     tmem_wait_ld();
     tc_fence_before();
-    mbar_arrive(&dq_free[0]);
+    mbar_arrive(dq_free);
     if (lane == 0 && warp == 4 && t > 0) bulk_wait_group_read0();
     named_bar_sync(2, 128);
 #pragma unroll
@@ -287,8 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_4d(sV, &tm_v, kv_full, 0, kt * BK, kvh, b);
       int issued = 0;
       for (int t = 0; t < NT; ++t) {
-        const int s = t & 1;
-        if (t >= 2 && !mbar_wait(&q_empty[s], ((t >> 1) - 1) & 1, abort_flag, err, 1)) break;
+        const int s = t % QS;
+        if (t >= QS && !mbar_wait(&q_empty[s], ((t / QS) - 1) & 1, abort_flag, err, 1)) break;
         int h, qt;
         tile_of(t, h, qt);
         const int64_t row = (int64_t)(b * p.heads + h) * p.nq_pad + qt * BQ;
@@ -301,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (*abort_flag) {
         drain_wait(kv_full, 0);
-        for (int t = max(0, issued - 2); t < issued; ++t) drain_wait(&q_full[t & 1], (t >> 1) & 1);
+        for (int t = max(0, issued - QS); t < issued; ++t) drain_wait(&q_full[t % QS], (t / QS) & 1);
       }
     }
   } else if (warp == 1) {
@@ -328,14 +337,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         issue_sdp(0);
       }
       for (int t = 0; ok && t < NT; ++t) {
-        const int s = t & 1;
+        const int s = t % QS;
+        if (t + 1 < NT) {
+          // S^T / dP^T of tile t are in the softmax threads' registers: the
+          // buffers take tile t + 1 while the softmax still works on t
+          if (!mbar_wait(sdp_free, t & 1, abort_flag, err, 11)) break;
+          if (!mbar_wait(&q_full[(t + 1) % QS], ((t + 1) / QS) & 1, abort_flag, err, 5)) break;
+          tc_fence_after();
+          issue_sdp((t + 1) % QS);
+        }
         if (!mbar_wait(p_ready, t & 1, abort_flag, err, 4)) break;
         tc_fence_after();
-        if (t + 1 < NT) {
-          if (!mbar_wait(&q_full[(t + 1) & 1], ((t + 1) >> 1) & 1, abort_flag, err, 5)) break;
-          tc_fence_after();
-          issue_sdp((t + 1) & 1);
-        }
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           const uint32_t aoff = (uint32_t)(kk >> 2) * (128 * 128) + (uint32_t)(kk & 3) * 32;
@@ -345,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_f16_ss(tmem + L::kDK, smem_desc_sw128(dsa + aoff, 16, 1024),
                      smem_desc_sw128(qa + s * L::kTile + kk * 2048, 128 * 128, 1024), idKV, acc);
         }
-        if (t >= 1 && !mbar_wait(&dq_free[0], (t - 1) & 1, abort_flag, err, 6)) break;
+        if (t >= 1 && !mbar_wait(dq_free, (t - 1) & 1, abort_flag, err, 6)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
@@ -354,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&q_empty[s]);
         mma_commit(mma_done);
-        mma_commit(&dq_full[0]);
+        mma_commit(dq_full);
       }
       mma_commit(dkv_done);
       mma_commit(drain);
@@ -378,29 +390,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     float dbias = 0.f;
     bool ok = true;
     for (int t = 0; t < NT && ok; ++t) {
-      const int s = t & 1;
+      const int s = t % QS;
       int h, qt;
       tile_of(t, h, qt);
       if (!mbar_wait_warp(sdp_full, t & 1, abort_flag, err, 7)) { ok = false; break; }
       tc_fence_after();
       const bool diag = p.causal && qt == kt;
-#pragma unroll 1
+      // the whole 64-query slice of S^T and dP^T into registers, then the
+      // TMEM buffers are released for tile t + 1
+      uint32_t sv[2][32], dv[2][32];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        tmem_ld32(tmem + lane_base + L::kS + (hw * 2 + cc) * 32, sv[cc]);
+        tmem_ld32(tmem + lane_base + L::kDP + (hw * 2 + cc) * 32, dv[cc]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(sdp_free);
+#pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c = hw * 2 + cc;
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tmem + lane_base + L::kS + c * 32, sv);
-        tmem_ld32(tmem + lane_base + L::kDP + c * 32, dv);
-        tmem_wait_ld();
         uint32_t pw[16], dw[16];
         const float* nl = sLse + s * BQ + c * 32;       // -lse2 of the chunk's queries
         const float* dl = sDel + s * BQ + c * 32;
         if (diag || !key_ok_warp)
-          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, true, DB>(sv, dv, nl, dl, b2, p, key_ok, c * 32, diag ? r : -1,
-                                                          dbias, pw, dw);
+          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, true, DB>(sv[cc], dv[cc], nl, dl, b2, p, key_ok, c * 32,
+                                                          diag ? r : -1, dbias, pw, dw);
         else
-          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, false, DB>(sv, dv, nl, dl, b2, p, key_ok, c * 32, -1, dbias, pw,
-                                                           dw);
-        // P^T / dS^T smem is free once the previous tile's MMAs completed
+          softmax_bwd_chunk<T, SOFTCLAMP, HAS_BIAS, false, DB>(sv[cc], dv[cc], nl, dl, b2, p, key_ok, c * 32, -1,
+                                                           dbias, pw, dw);
+        // P^T (TMEM) / dS^T (smem) are free once the previous tile's MMAs completed
         if (cc == 0 && t > 0 && !mbar_wait_warp(mma_done, (t - 1) & 1, abort_flag, err, 8)) {
           ok = false;
           break;
