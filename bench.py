@@ -432,6 +432,7 @@ def run_decode(args, dev):
     ms = s.elapsed_time(e)
     _, _, hbm, kind = peaks()
     gbs = total_bytes / (ms * 1e-3) / 1e9
+    module_step = run_module_decode(args, dev, b, L0, steps) if (b, L0) == (32, 2048) else None
     return {"metric": "decode tok/s", "value": b * steps / (ms * 1e-3), "unit": "tokens/s", "steps": steps,
             "ms_per_step": ms / steps, "config": {"workload": "NPolyAttention order 3 core decode (config 4)"
                                                   if (b, L0) == (32, 2048) else "NPolyAttention order 3 core decode",
@@ -440,7 +441,40 @@ def run_decode(args, dev):
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                          "traffic": None, "peak_kind": f"{kind} copy bandwidth",
                          "bytes_note": "7 bf16 cache tensors + 2 fp32 lse caches at kv-head width per position"},
-            "clocks": clk.summary(), "gpu_launches": int(_lib.launch_count() - n0)}
+            "clocks": clk.summary(), "gpu_launches": int(_lib.launch_count() - n0), "module_step": module_step}
+
+
+def run_module_decode(args, dev, b, L0, steps):
+    """The same decode through the drop-in module: NPolyAttention(dim=2048,
+    order=3, heads=16, kv_heads=4, dim_head=128, causal=True) prefilled with
+    L0 tokens (return_cache=True), then `steps` single-token calls each
+    passing back the returned cache tuple (appended in place). Includes the
+    projections, q-norms and output projection of every step."""
+    import torch
+
+    import poly_attention_b200 as P
+    torch.manual_seed(0)
+    m = P.NPolyAttention(dim=2048, order=3, heads=16, kv_heads=4, dim_head=128, causal=True).to(dev, torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(78)
+    x = torch.randn(b, L0 + steps + 3, 2048, device=dev, dtype=torch.bfloat16, generator=g)
+    with torch.no_grad():
+        _, cache0 = m(x[:, :L0], return_cache=True)
+        c = cache0
+        for i in range(3):                         # warm-up steps on a branch of the cache
+            _, c = m(x[:, L0 + i:L0 + i + 1], cache=c, return_cache=True)
+        _, c = m(x[:, :L0], return_cache=True)     # fresh prefill, then the timed steps
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(steps):
+            _, c = m(x[:, L0 + i:L0 + i + 1], cache=c, return_cache=True)
+        e.record()
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    del m, x, c, cache0
+    return {"api": "NPolyAttention.forward(x_t, cache=..., return_cache=True)", "ms_per_step": ms,
+            "value": b / (ms * 1e-3), "unit": "tokens/s",
+            "note": "whole module step: projections, q-norms, in-place cache append, decode kernels, to_out"}
 
 
 LONGCTX = (1, 16, 32768, 64)

@@ -12,6 +12,7 @@
 // O_B [320,384), P_A [384,448), P_B [448,512). P (16-bit, two per column)
 // stays in TMEM and is the A operand of the P V MMA, so no probability tile
 // crosses shared memory (shared-memory operand bandwidth bounds SS MMAs).
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -61,6 +62,7 @@ struct L2T {
 
 struct Fwd2Params {
   int seq_q, seq_k, heads, kv_heads, m_tiles, causal;
+  int n_bh, grp_bh;   // batch * heads; (batch, head) units per dispatch group
   float sl2, scale;
   void* out; int64_t out_stride[3];
   float* lse; int64_t lse_stride[2];
@@ -129,11 +131,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* err = g_poly_device_error;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // grid: x = (batch, head), y = query-tile pair, heaviest (most key tiles)
-  // first, so the dispatch order is longest-first across all heads
-  const int b = blockIdx.x / p.heads, h = blockIdx.x - b * p.heads;
+  // 1-D grid over groups of grp_bh consecutive (batch, head) units (whole GQA
+  // groups, sized so their K / V stay in L2 together); inside a group the
+  // query-tile pairs go heaviest (most key tiles) first, every unit of the
+  // group at one pair index before the next, so the dispatch is
+  // longest-first while the CTAs in flight share few K / V streams
+  int bh, yi;
+  {
+    const int lin = blockIdx.x;
+    const int grp = lin / (p.grp_bh * p.m_tiles);
+    const int gsz = min(p.grp_bh, p.n_bh - grp * p.grp_bh);
+    const int rem = lin - grp * p.grp_bh * p.m_tiles;
+    yi = rem / gsz;
+    bh = grp * p.grp_bh + (rem - yi * gsz);
+  }
+  const int b = bh / p.heads, h = bh - b * p.heads;
   const int kvh = h / (p.heads / p.kv_heads);
-  const int mt = p.causal ? (p.m_tiles - 1 - (int)blockIdx.y) : (int)blockIdx.y;
+  const int mt = p.causal ? (p.m_tiles - 1 - yi) : yi;
   const int row0 = mt * 2 * BM;
   const int kt_total = (p.seq_k + BN - 1) / BN;
   // key tiles seen by tile A (rows row0..) and tile B (rows row0 + 128..)
@@ -465,7 +479,14 @@ int launch_t(const PolyPassArgs& a, cudaStream_t st) {
   }
   p.lse_stride[0] = a.lse_stride[0];
   p.lse_stride[1] = a.lse_stride[1];
-  dim3 grid(a.batch * a.heads, p.m_tiles);
+  // dispatch groups: whole GQA groups whose K / V (2 x seq_k x D x 2 bytes per
+  // kv head) fit in ~32 MB of L2
+  const int rep_h = a.heads / a.kv_heads;
+  const size_t kv_bytes = (size_t)a.seq_k * D * 4;
+  const int grp_kv = (int)std::max<size_t>(1, (32u << 20) / std::max<size_t>(kv_bytes, 1));
+  p.n_bh = a.batch * a.heads;
+  p.grp_bh = std::min(p.n_bh, grp_kv * rep_h);
+  dim3 grid((unsigned)(p.n_bh * p.m_tiles));
   pass_fwd_tc2_kernel<T, HAS_BIAS, D><<<grid, kThreads, L2::kAlloc, st>>>(tq, tk, tv, tb, p);
   note_launch(1);
   return cuda_status(cudaGetLastError(), "pass_fwd_tc2 launch");

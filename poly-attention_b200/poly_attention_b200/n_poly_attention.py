@@ -13,6 +13,7 @@ from torch.nn import Module, RMSNorm
 
 from .core import poly_attention_chain, poly_attention_chain_cached
 from .head_norm import head_rmsnorm
+from .kv_cache import ModuleKVCache, usable as _inplace_usable
 from .poly_attention import _rotary, cast_tuple, default, exists, merge_heads, split_heads
 
 LinearNoBias = partial(nn.Linear, bias=False)
@@ -54,9 +55,22 @@ class NPolyAttention(Module):
         self.q_norms = nn.ModuleList([RMSNorm(dim_head) for _ in range(order + 1)])
         self.rotary_emb = _rotary().RotaryEmbedding(dim_head) if use_rotary_embed else None
         self.to_out = nn.Linear(dim_inner, dim)
+        # buffers behind the cache tuple returned last (in-place decoding steps)
+        self._kv_cache = None
 
     def _expand(self, t):
         return t if (t is None or self.num_rep == 1) else t.repeat_interleave(self.num_rep, dim=1)
+
+    def _finish(self, out, root_value, gates):
+        """Root-value / attention gates, merge heads, output projection
+        (n_poly_attention.py:315-328)."""
+        if self.multiply_root_value:
+            if self.use_root_value_as_attn_gate:
+                root_value = root_value.sigmoid()
+            out = self._expand(root_value) * out
+        if self.attn_gate:
+            out = out * gates.sigmoid()
+        return self.to_out(merge_heads(out))
 
     def _squeeze(self, t):
         return t if (t is None or self.num_rep == 1) else t[:, ::self.num_rep]
@@ -108,6 +122,26 @@ class NPolyAttention(Module):
             qs = tuple(r.apply_rotary_emb(rotary_pos_emb, q) for q in qs)
         q1, qs_rest = qs[0], qs[1:]
 
+        inplace = (_inplace_usable(q1.dtype, q1.device, self.dim_head, exists(mask) or any(exists(m) for m in context_mask),
+                                   exists(rotary_pos_emb) or exists(self.rotary_emb))
+                   and (not has_cache or all(torch.is_tensor(t) and t.dtype == q1.dtype
+                                             for part in cache for t in part)))
+        if has_cache and inplace:
+            # append in place to the module's cache buffers (a copy first if
+            # the tuple is not the one this module returned last)
+            c_qs, c_vs, c_lses, c_msgs = cache
+            kv = self._kv_cache
+            if kv is None or not kv.owns(list(c_qs), list(c_vs), list(c_lses), list(c_msgs)):
+                kv = ModuleKVCache.from_tuple(list(c_qs), list(c_vs), list(c_lses), list(c_msgs), heads=self.heads,
+                                              softclamp_value=self.softclamp_value)
+            if kv.length >= kv.cap:
+                kv = kv.grown()
+            self._kv_cache = kv
+            out = self._finish(kv.step(q1, list(qs_rest), list(vs)), root_value, gates)
+            if not return_cache:
+                return out
+            k, v, l, m = kv.views()
+            return out, (tuple(k), tuple(v), tuple(l), tuple(m))
         if has_cache:
             c_qs, c_vs, c_lses, c_msgs = cache
         else:
@@ -132,15 +166,16 @@ class NPolyAttention(Module):
                 q_left, q_right, list(vs_cache), softclamp_value=self.softclamp_value, causal=self.causal,
                 mask=mask, context_masks=context_mask)
 
-        if self.multiply_root_value:
-            if self.use_root_value_as_attn_gate:
-                root_value = root_value.sigmoid()
-            out = self._expand(root_value) * out
-        if self.attn_gate:
-            out = out * gates.sigmoid()
-        out = self.to_out(merge_heads(out))
+        out = self._finish(out, root_value, gates)
         if not return_cache:
             return out
+        if inplace and not has_cache:
+            # prefill: the returned cache lives in buffers later steps append to
+            kv = ModuleKVCache.from_core(list(qs_rest_cache), list(vs_cache), list(lse_steps), list(msg_steps),
+                                         heads=self.heads, softclamp_value=self.softclamp_value)
+            self._kv_cache = kv
+            k, v, l, m = kv.views()
+            return out, (tuple(k), tuple(v), tuple(l), tuple(m))
         new_lses, new_msgs = [], []
         for i, (l, m) in enumerate(zip(lse_steps, msg_steps)):
             l = self._expand(l).to(out.dtype)

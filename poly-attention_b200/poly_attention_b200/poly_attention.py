@@ -14,6 +14,7 @@ from torch.nn import Module, RMSNorm
 
 from .core import poly_attention_order2, poly_attention_order2_cached
 from .head_norm import head_rmsnorm
+from .kv_cache import ModuleKVCache, usable as _inplace_usable
 
 LinearNoBias = partial(nn.Linear, bias=False)
 
@@ -87,6 +88,19 @@ class Order2PolyAttention(Module):
         self.q_norms = nn.ModuleList([RMSNorm(dim_head), RMSNorm(dim_head), RMSNorm(dim_head)])
         self.rotary_emb = _rotary().RotaryEmbedding(dim_head) if use_rotary_embed else None
         self.to_out = nn.Linear(dim_inner, dim)
+        # buffers behind the cache tuple returned last (in-place decoding steps)
+        self._kv_cache = None
+
+    def _finish(self, out, v2, gates):
+        """Root-value / attention gates, merge heads, output projection
+        (poly_attention/poly_attention.py:342-355)."""
+        if self.multiply_root_value:
+            if self.use_root_value_as_attn_gate:
+                v2 = v2.sigmoid()
+            out = self._expand(v2) * out
+        if self.attn_gate:
+            out = out * gates.sigmoid()
+        return self.to_out(merge_heads(out))
 
     def _expand(self, t):
         # [b, g, ...] -> [b, h, ...] as 'b g ... -> b (g r) ...'
@@ -142,6 +156,26 @@ class Order2PolyAttention(Module):
             q1, q2, q3 = (r.apply_rotary_emb(rotary_pos_emb, q) for q in (q1, q2, q3))
 
         cq2, cq3, cv3, clse23, cmsg = cache if has_cache else (None,) * 5
+        inplace = (_inplace_usable(q1.dtype, q1.device, self.dim_head,
+                                   exists(mask) or any(exists(m) for m in context_mask),
+                                   exists(rotary_pos_emb) or exists(self.rotary_emb))
+                   and (not has_cache or all(torch.is_tensor(t) and t.dtype == q1.dtype for t in cache)))
+        if has_cache and inplace:
+            # append in place to the module's cache buffers (a copy first if
+            # the tuple is not the one this module returned last)
+            kv = self._kv_cache
+            if kv is None or not kv.owns([cq2, cq3], [cv3], [clse23], [cmsg]):
+                kv = ModuleKVCache.from_tuple([cq2, cq3], [cv3], [clse23], [cmsg], heads=self.heads,
+                                              softclamp_value=self.softclamp_value)
+            if kv.length >= kv.cap:
+                kv = kv.grown()
+            self._kv_cache = kv
+            out = kv.step(q1, [q2, q3], [v3])
+            out = self._finish(out, v2, gates)
+            if not return_cache:
+                return out
+            k, v, l, m = kv.views()
+            return out, (k[0], k[1], v[0], l[0], m[0])
         cat = lambda c, t: t if c is None else torch.cat((c, t), dim=-2)  # noqa: E731
         q2_cache, q3_cache, v3_cache = cat(cq2, q2), cat(cq3, q3), cat(cv3, v3)
 
@@ -161,15 +195,16 @@ class Order2PolyAttention(Module):
                 q1, q2_right, q3_full, v3_cache, q2_pass1=q2_pass1, mask=mask, context_mask=context_mask,
                 softclamp_value=self.softclamp_value, causal=self.causal)
 
-        if self.multiply_root_value:
-            if self.use_root_value_as_attn_gate:
-                v2 = v2.sigmoid()
-            out = self._expand(v2) * out
-        if self.attn_gate:
-            out = out * gates.sigmoid()
-        out = self.to_out(merge_heads(out))
+        out = self._finish(out, v2, gates)
         if not return_cache:
             return out
+        if inplace and not has_cache:
+            # prefill: the returned cache lives in buffers later steps append to
+            kv = ModuleKVCache.from_core([q2_cache, q3_cache], [v3_cache], [lse_step], [msg_step], heads=self.heads,
+                                         softclamp_value=self.softclamp_value)
+            self._kv_cache = kv
+            k, v, l, m = kv.views()
+            return out, (k[0], k[1], v[0], l[0], m[0])
         lse_step = self._expand(lse_step).to(out.dtype)
         msg_step = self._expand(msg_step)
         lse23_full = lse_step if clse23 is None else torch.cat((clse23, lse_step), dim=-1)
