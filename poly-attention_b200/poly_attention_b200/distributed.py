@@ -3,26 +3,27 @@
 One process per GPU (torch.distributed, NCCL). The sequence of n rows is cut
 into 2P chunks of C = n / (2P) rows; rank r owns chunks r and 2P-1-r
 ("zig-zag", which balances the causal work). Each rank holds the rows of its
-chunks of q1, q2, q3, v3 (``[b, h, 2C, d]``, chunk r first).
+chunks of q1, q2, q3, v3 (``[b, h, 2C, d]``, chunk r first) and produces the
+output rows of those chunks.
 
 Forward (causal, reference semantics of poly_attention/poly_attention.py:48-116):
 
-1. all-gather q1, q3, v3 (q2 stays local: pass 1's queries and pass 2's keys
-   are the rank's own rows).
-2. pass 1 for the own rows: keys of earlier chunks without mask plus the
-   diagonal chunk with the causal mask, merged by log-sum-exp -> (msg, lse23)
-   of the own rows, complete: pass-1 rows are exactly pass-2 keys.
-3. pass 2, key split: for each own key chunk c, the queries of chunk c
-   (causal) and of every later chunk (no mask) attend keys c with lse23 as key
-   bias, as one causal call -> partial (out, lse) for every query row; the two
-   own chunks are merged locally (poly_lse_merge).
-4. the one exchange: all-reduce(max) of the partial lse per row, each rank
-   rescales its partial by exp(lse - max), then reduce-scatter(sum) of
-   [acc | l] (fp32) delivers every row's totals to its owner, which divides.
+1. start all-gathers of q3, v3 (pass 1's keys / values) and q2 (pass 2's
+   keys); the q2 gather runs while pass 1 computes.
+2. pass 1 for the own rows of q2: the keys of earlier chunks without mask plus
+   the diagonal chunk with the causal mask, merged by log-sum-exp -> (msg,
+   lse23) of the own rows, complete (pass-1 rows are exactly pass-2 keys).
+3. all-gather msg and lse23: every rank now holds pass 2's keys (q2), values
+   (msg) and key bias (lse23) for the whole sequence.
+4. pass 2 for the own rows of q1, the same prefix + diagonal split: complete
+   output rows, no partial results leave the rank.
 
-The attention passes are the CUDA kernels (``ops.pass_fwd`` / ``ops.lse_merge``);
-``pass_fn`` / ``merge_fn`` can be replaced, which the CPU tests use to check
-the collective logic with the gloo backend.
+Per rank this receives 4 (n x d) 16-bit tensors and one n-row fp32 vector
+(times (P - 1) / P) and never sends q1; the compute is 2 x n x 2C key-query
+pairs per pass (balanced by the zig-zag). The attention passes are the CUDA
+kernels (``ops.pass_fwd`` / ``ops.lse_merge``); ``pass_fn`` / ``merge_fn`` can
+be replaced, which the CPU tests use to check the collective logic with the
+gloo backend.
 """
 from __future__ import annotations
 
@@ -55,13 +56,24 @@ def zigzag_unshard(parts, world: int, dim: int = -2) -> torch.Tensor:
     return torch.cat(chunks, dim=dim)
 
 
-def _gather_full(x_loc, world, group):
-    """all-gather zig-zag shards and reassemble the natural row order."""
+def _gather_start(x_loc, world, group):
+    """Start an all-gather of this rank's zig-zag shard; returns a handle for
+    _gather_finish (no collective at world size 1)."""
+    x_loc = x_loc.contiguous()
     if world == 1:
-        return zigzag_unshard([x_loc], 1)
+        return [x_loc], None
     parts = [torch.empty_like(x_loc) for _ in range(world)]
-    dist.all_gather(parts, x_loc.contiguous(), group=group)
-    return zigzag_unshard(parts, world)
+    work = dist.all_gather(parts, x_loc, group=group, async_op=True)
+    return parts, work
+
+
+def _gather_finish(handle, world, dim=-2):
+    """Wait for the gather (stream-ordered with NCCL) and reassemble the
+    natural row order along `dim`."""
+    parts, work = handle
+    if work is not None:
+        work.wait()
+    return parts[0] if world == 1 else zigzag_unshard(parts, world, dim=dim)
 
 
 def _default_ops():
@@ -82,56 +94,38 @@ def context_parallel_order2_fwd(q1_loc, q2_loc, q3_loc, v3_loc, *, group=None, s
         merge_fn = merge_fn or mf
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
-    b, h, n2, d = q1_loc.shape
-    C = n2 // 2
-    n = C * 2 * world
-    ca, cb = zigzag_chunks(rank, world)
-    own = (ca, cb)
+    C = q1_loc.shape[-2] // 2
+    own = zigzag_chunks(rank, world)
+    sc = softclamp_value
 
-    q1 = _gather_full(q1_loc, world, group)
-    q3 = _gather_full(q3_loc, world, group)
-    v3 = _gather_full(v3_loc, world, group)
-    rows = lambda x, c: x[:, :, c * C:(c + 1) * C]  # noqa: E731
+    h_q3 = _gather_start(q3_loc, world, group)
+    h_v3 = _gather_start(v3_loc, world, group)
+    h_q2 = _gather_start(q2_loc, world, group)
 
-    # 2. pass 1 for the own rows (keys <= row): earlier chunks unmasked + diagonal causal
-    msgs, lses = [], []
-    for k, c in enumerate(own):
-        q2c = q2_loc[:, :, k * C:(k + 1) * C]
-        o_d, l_d = pass_fn(q2c, rows(q3, c), rows(v3, c), causal=True, softclamp=softclamp_value)
+    def attend(q_rows, c, k, v, bias):
+        """Rows of chunk c attend keys [0, (c + 1) C): the diagonal chunk with
+        the causal mask (both index ranges start at c * C, so the top-left
+        rule is exact) and the earlier chunks unmasked, merged."""
+        o, l = pass_fn(q_rows, k[:, :, c * C:(c + 1) * C], v[:, :, c * C:(c + 1) * C], causal=True, softclamp=sc,
+                       bias=None if bias is None else bias[:, :, c * C:(c + 1) * C])
         if c > 0:
-            o_p, l_p = pass_fn(q2c, q3[:, :, :c * C], v3[:, :, :c * C], causal=False, softclamp=softclamp_value)
-            o_d, l_d = merge_fn(torch.stack([o_p, o_d]), torch.stack([l_p, l_d]))
-        msgs.append(o_d)
-        lses.append(l_d)
+            o_p, l_p = pass_fn(q_rows, k[:, :, :c * C], v[:, :, :c * C], causal=False, softclamp=sc,
+                               bias=None if bias is None else bias[:, :, :c * C])
+            o, l = merge_fn(torch.stack([o_p, o]), torch.stack([l_p, l]))
+        return o, l
 
-    # 3. pass 2 partials for every query row from the own key chunks. Queries
-    # from chunk c on against keys of chunk c is one causal call: with both
-    # index ranges starting at c * C, the top-left causal rule masks exactly
-    # the diagonal block and leaves the later rows unmasked.
-    part_out = torch.empty(2, b, h, n, d, device=q1.device, dtype=q1.dtype)
-    part_lse = torch.empty(2, b, h, n, device=q1.device, dtype=torch.float32)
-    for k, c in enumerate(own):
-        q2c = q2_loc[:, :, k * C:(k + 1) * C]
-        o, l = pass_fn(q1[:, :, c * C:], q2c, msgs[k], causal=True, softclamp=softclamp_value, bias=lses[k])
-        part_out[k, :, :, c * C:] = o
-        part_lse[k, :, :, c * C:] = l
-        part_out[k, :, :, :c * C] = 0        # rows before chunk c see none of its keys
-        part_lse[k, :, :, :c * C] = -math.inf
-    out_p, lse_p = merge_fn(part_out, part_lse)
+    # pass 1 for the own rows of q2 (poly_attention/poly_attention.py:63-82)
+    q3 = _gather_finish(h_q3, world)
+    v3 = _gather_finish(h_v3, world)
+    res = [attend(q2_loc[:, :, k * C:(k + 1) * C], c, q3, v3, None) for k, c in enumerate(own)]
+    del q3, v3
+    h_msg = _gather_start(torch.cat([r[0] for r in res], dim=-2), world, group)
+    h_lse = _gather_start(torch.cat([r[1] for r in res], dim=-1), world, group)
+    del res
 
-    # 4. exchange: max of lse, then sum of rescaled [acc | l] to the row owners
-    m = lse_p.clone()
-    if world > 1:
-        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
-    w = torch.where(torch.isfinite(lse_p), torch.exp(lse_p - m), torch.zeros_like(lse_p))
-    buf = torch.cat([out_p.float() * w[..., None], w[..., None]], dim=-1)           # [b, h, n, d + 1]
-    # zig-zag order so that reduce-scatter's contiguous blocks are the owners' rows
-    blocks = [zigzag_shard(buf, r, world) for r in range(world)]
-    if world > 1:
-        mine = torch.empty_like(blocks[0])
-        dist.reduce_scatter(mine, [x.contiguous() for x in blocks], op=dist.ReduceOp.SUM, group=group)
-    else:
-        mine = blocks[0]
-    acc, l = mine[..., :d], mine[..., d:]
-    out = torch.where(l > 0, acc / l.clamp_min(1e-30), torch.zeros_like(acc))
-    return out.to(q1_loc.dtype)
+    # pass 2 for the own rows of q1, lse23 as key bias (:91-114)
+    q2 = _gather_finish(h_q2, world)
+    msg = _gather_finish(h_msg, world)
+    lse23 = _gather_finish(h_lse, world, dim=-1)
+    outs = [attend(q1_loc[:, :, k * C:(k + 1) * C], c, q2, msg, lse23)[0] for k, c in enumerate(own)]
+    return torch.cat(outs, dim=-2).to(q1_loc.dtype)

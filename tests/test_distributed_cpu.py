@@ -1,5 +1,6 @@
-"""Key-split long-context order-2 forward: the sharding, all-gather, partial
-passes and the max / reduce-scatter exchange, run as gloo ranks on CPU with
+"""Key-split long-context order-2 forward: the sharding, the all-gathers of
+q2 / q3 / v3 and of pass 1's (msg, lse), and the per-rank passes, run as gloo
+ranks on CPU with
 the attention passes supplied by the oracle (the CUDA kernels are checked by
 the GPU tests). Must equal the oracle's full-sequence causal forward."""
 import math
