@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define POLY_ABI_VERSION 1
+#define POLY_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define POLY_API __attribute__((visibility("default")))
@@ -105,6 +105,17 @@ typedef struct PolyPassArgs {
 
   void* workspace;          /* device scratch, >= poly_pass_fwd_workspace_size() bytes */
   size_t workspace_bytes;
+
+  /* With causal: key j visible to query i iff j <= i + causal_offset, i.e. the
+   * queries are rows [causal_offset, causal_offset + seq_q) of a longer
+   * sequence whose first seq_k keys are given (no counterpart in the
+   * reference: it lets one launch cover a sequence shard's queries against
+   * all earlier keys). 0 is the reference's top-left causal mask. Non-zero
+   * values must be multiples of 128 and are taken by the tcgen05 forward only
+   * (bf16 / fp16, head_dim 64 or 128, no masks, no softclamp); elsewhere
+   * POLY_EUNSUPPORTED. Negative: POLY_EINVAL. */
+  int32_t causal_offset;
+  int32_t reserved_;
 } PolyPassArgs;
 
 /*

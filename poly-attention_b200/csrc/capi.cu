@@ -31,12 +31,15 @@ static int check_pass(const PolyPassArgs* a) {
   if (!a->q || !a->k || !a->v || !a->out) return fail(POLY_EINVAL, "q, k, v and out are required");
   if (a->epi_out && !a->epi_mul) return fail(POLY_EINVAL, "epi_out requires epi_mul");
   if (!(a->scale == a->scale)) return fail(POLY_EINVAL, "scale is NaN");
+  if (a->causal_offset < 0) return fail(POLY_EINVAL, "causal_offset must be non-negative");
   return POLY_OK;
 }
 
 enum class FwdKind { kSimt, kTc, kDecode, kSmall, kF32 };
 
 static FwdKind choose_fwd(const PolyPassArgs& a) {
+  // a causal offset only on the tcgen05 forward (kSimt is then refused by the caller)
+  if (a.causal_offset) return pass_fwd_tc_eligible(a) && pass_fwd_tc2_eligible(a) ? FwdKind::kTc : FwdKind::kSimt;
   if (pass_decode_eligible(a)) return FwdKind::kDecode;
   if (pass_small_eligible(a)) return FwdKind::kSmall;
   if (pass_f32_eligible(a)) return FwdKind::kF32;
@@ -104,6 +107,9 @@ int poly_pass_fwd(const PolyPassArgs* a, void* stream) {
   if (rc) return rc;
   if (a->seq_q == 0) return POLY_OK;
   const FwdKind kind = choose_fwd(*a);
+  if (a->causal_offset && (kind != FwdKind::kTc || !a->causal || (a->causal_offset % 128) != 0))
+    return fail(POLY_EUNSUPPORTED, "causal_offset needs causal, a multiple of 128 and the tcgen05 forward "
+                                   "(bf16 / fp16, head_dim 64 or 128, no masks, no softclamp)");
   size_t need = 0;
   if (kind == FwdKind::kDecode) need = pass_decode_workspace(*a);
   if (kind == FwdKind::kTc) need = pass_fwd_tc_workspace(*a);
@@ -164,6 +170,7 @@ int poly_pass_bwd(const PolyPassBwdArgs* a, void* stream) {
   int rc = check_pass(&a->fwd);
   if (rc) return rc;
   if (a->fwd.v_mul) return fail(POLY_EUNSUPPORTED, "v_mul is forward-only");
+  if (a->fwd.causal_offset) return fail(POLY_EUNSUPPORTED, "causal_offset is forward-only");
   if (!a->fwd.lse || !a->dout || !a->dq || !a->dk || !a->dv)
     return fail(POLY_EINVAL, "backward needs fwd.out, fwd.lse, dout, dq, dk and dv");
   const bool tc = use_bwd_tc(*a);

@@ -62,6 +62,7 @@ struct L2T {
 
 struct Fwd2Params {
   int seq_q, seq_k, heads, kv_heads, m_tiles, causal;
+  int off_tiles;      // causal offset in 128-key tiles
   int n_bh, grp_bh;   // batch * heads; (batch, head) units per dispatch group
   float sl2, scale;
   void* out; int64_t out_stride[3];
@@ -151,8 +152,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int row0 = mt * 2 * BM;
   const int kt_total = (p.seq_k + BN - 1) / BN;
   // key tiles seen by tile A (rows row0..) and tile B (rows row0 + 128..)
-  const int ntA = p.causal ? min(kt_total, 2 * mt + 1) : kt_total;
-  const int ntB = p.causal ? min(kt_total, 2 * mt + 2) : kt_total;
+  const int ntA = p.causal ? min(kt_total, 2 * mt + 1 + p.off_tiles) : kt_total;
+  const int ntB = p.causal ? min(kt_total, 2 * mt + 2 + p.off_tiles) : kt_total;
   const int ntMax = ntB;
 
   if (threadIdx.x == 0) {
@@ -279,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const int nt = x == 0 ? ntA : ntB;
-    const int diag_tile = 2 * mt + x;             // causal: the key tile on this tile's diagonal
+    const int diag_tile = 2 * mt + x + p.off_tiles;  // causal: the key tile on this tile's diagonal
     const uint32_t s_addr = tmem + lane_base + x * BN;
     const uint32_t o_addr = tmem + lane_base + 256 + x * D;
     const uint32_t p_addr = tmem + lane_base + (kAlias ? x * BN : 384 + x * 64);
@@ -466,6 +467,7 @@ int launch_t(const PolyPassArgs& a, cudaStream_t st) {
   p.kv_heads = a.kv_heads;
   p.m_tiles = (a.seq_q + 2 * BM - 1) / (2 * BM);
   p.causal = a.causal;
+  p.off_tiles = a.causal ? a.causal_offset / BN : 0;
   p.sl2 = a.scale * kLog2e;
   p.scale = a.scale;
   p.out = a.out;

@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(_HERE, "libpolyattn.so")
 
 POLY_OK, POLY_EINVAL, POLY_EUNSUPPORTED, POLY_ECUDA = 0, 1, 2, 3
 POLY_F32, POLY_F16, POLY_BF16 = 0, 1, 2
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 c_i32, c_i64, c_f32, c_vp, c_sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 I64x3 = c_i64 * 3
@@ -36,6 +36,7 @@ class PolyPassArgs(ctypes.Structure):
         ("epi_mul", c_vp), ("epi_mul_stride", I64x3),
         ("epi_out", c_vp), ("epi_out_stride", I64x3),
         ("workspace", c_vp), ("workspace_bytes", c_sz),
+        ("causal_offset", c_i32), ("reserved_", c_i32),
     ]
 
 

@@ -10,13 +10,15 @@ Forward (causal, reference semantics of poly_attention/poly_attention.py:48-116)
 
 1. start all-gathers of q3, v3 (pass 1's keys / values) and q2 (pass 2's
    keys); the q2 gather runs while pass 1 computes.
-2. pass 1 for the own rows of q2: the keys of earlier chunks without mask plus
-   the diagonal chunk with the causal mask, merged by log-sum-exp -> (msg,
-   lse23) of the own rows, complete (pass-1 rows are exactly pass-2 keys).
+2. pass 1 for the own rows of q2 against every key up to the row: one causal
+   launch with the key index offset by the chunk start (or, for chunks not a
+   multiple of 128 rows, the earlier chunks unmasked plus the diagonal chunk
+   causal, merged by log-sum-exp) -> (msg, lse23) of the own rows, complete
+   (pass-1 rows are exactly pass-2 keys).
 3. all-gather msg and lse23: every rank now holds pass 2's keys (q2), values
    (msg) and key bias (lse23) for the whole sequence.
-4. pass 2 for the own rows of q1, the same prefix + diagonal split: complete
-   output rows, no partial results leave the rank.
+4. pass 2 for the own rows of q1, the same way: complete output rows, no
+   partial results leave the rank.
 
 Per rank this receives 4 (n x d) 16-bit tensors and one n-row fp32 vector
 (times (P - 1) / P) and never sends q1; the compute is 2 x n x 2C key-query
@@ -103,9 +105,14 @@ def context_parallel_order2_fwd(q1_loc, q2_loc, q3_loc, v3_loc, *, group=None, s
     h_q2 = _gather_start(q2_loc, world, group)
 
     def attend(q_rows, c, k, v, bias):
-        """Rows of chunk c attend keys [0, (c + 1) C): the diagonal chunk with
-        the causal mask (both index ranges start at c * C, so the top-left
-        rule is exact) and the earlier chunks unmasked, merged."""
+        """Rows of chunk c attend keys [0, (c + 1) C). With C a multiple of the
+        128-key tile this is one causal launch whose key index is offset by
+        c * C; otherwise the diagonal chunk with the causal mask (both index
+        ranges start at c * C, so the top-left rule is exact) and the earlier
+        chunks unmasked, merged."""
+        if c > 0 and C % 128 == 0:
+            return pass_fn(q_rows, k[:, :, :(c + 1) * C], v[:, :, :(c + 1) * C], causal=True, softclamp=sc,
+                           bias=None if bias is None else bias[:, :, :(c + 1) * C], causal_offset=c * C)
         o, l = pass_fn(q_rows, k[:, :, c * C:(c + 1) * C], v[:, :, c * C:(c + 1) * C], causal=True, softclamp=sc,
                        bias=None if bias is None else bias[:, :, c * C:(c + 1) * C])
         if c > 0:

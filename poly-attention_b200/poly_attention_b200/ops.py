@@ -90,8 +90,11 @@ def _fill_pass(a: PolyPassArgs, q, k, v, out, lse, *, causal, softclamp, scale, 
 
 @torch.compiler.disable   # library calls through ctypes: dynamo runs them eagerly
 def pass_fwd(q, k, v, *, causal=False, softclamp=None, scale=None, bias=None, key_mask=None, query_mask=None,
-             epi_mul=None, v_mul=None, out=None, lse=None, want_lse=True):
+             epi_mul=None, v_mul=None, out=None, lse=None, want_lse=True, causal_offset=0):
     """One attention pass (see PolyPassArgs in include/poly_attention.h).
+
+    ``causal_offset`` (with causal, a multiple of 128): key j is visible to
+    query i iff j <= i + causal_offset.
 
     ``v_mul`` (same shape as v) multiplies the values elementwise inside the
     kernel; ``epi_mul`` (shape of out) makes the kernel also return epi_mul * out.
@@ -112,6 +115,7 @@ def pass_fwd(q, k, v, *, causal=False, softclamp=None, scale=None, bias=None, ke
     keep = []
     _fill_pass(a, q, k, v, out, lse, causal=causal, softclamp=softclamp, scale=scale, bias=bias, key_mask=key_mask,
                query_mask=query_mask, epi_mul=epi_mul, epi_out=epi_out, keep=keep, v_mul=v_mul)
+    a.causal_offset = int(causal_offset)
     ws_bytes = lib.poly_pass_fwd_workspace_size(ctypes.byref(a))
     ws = None
     if ws_bytes:

@@ -407,3 +407,32 @@ def test_order2_pass1_mask_fully_masking_a_sequence(causal):
                                         context_mask=(None, torch.as_tensor(cm2).cuda()), causal=causal)
     eo, _, _ = O.order2_fwd(q1, q2, q2, q3, v3, context_mask=(None, cm2), causal=causal)
     assert_close(out, eo, dtype, "out")
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("off,nq,nk", [(128, 256, 384), (256, 300, 556), (512, 128, 600)])
+def test_pass_fwd_causal_offset(d, off, nq, nk):
+    """causal_offset: the queries are rows [off, off + nq) of the key sequence
+    (key j visible iff j <= i + off); equals the oracle's top-left causal pass
+    over the whole sequence, restricted to those rows."""
+    import poly_attention_b200 as P
+    b, h = 2, 4
+    dt = torch.bfloat16
+    qf = quant(rnd((b, h, off + nq, d), 1), dt)
+    k, v = (quant(rnd((b, h, nk, d), i + 2), dt) for i in range(2))
+    bias = rnd((b, h, nk), 9)
+    out, lse = P.pass_fwd(dev(qf[:, :, off:], dt), dev(k, dt), dev(v, dt), causal=True, bias=dev(bias),
+                          causal_offset=off)
+    assert P.kernel_names(dev(qf[:, :, off:], dt), dev(k, dt), dev(v, dt), causal=True)[0] == "tc100"
+    eo, el = O.pass_fwd(qf, k, v, causal=True, bias=bias)
+    assert_close(out, eo[:, :, off:], dt, "out")
+    assert_close(lse, el[:, :, off:], dt, "lse")
+
+
+def test_pass_fwd_causal_offset_rejected_where_unsupported():
+    import poly_attention_b200 as P
+    q = torch.randn(1, 2, 256, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(Exception):
+        P.pass_fwd(q, q, q, causal=True, causal_offset=100)        # not a multiple of 128
+    with pytest.raises(Exception):
+        P.pass_fwd(q.float(), q.float(), q.float(), causal=True, causal_offset=128)   # fp32 kernel
