@@ -58,8 +58,8 @@ def pass_fwd_flop(b):
 
 # DRAM bytes per launch per batch element, from the ncu captures summarised in
 # profiles/ (batch-1 case; traffic scales with batch: every (b, h) reads its own
-# q/k/v once). pass_fwd_tc2: read 25.2 MB; pass_bwd_tc: read 50.9 MB.
-TRAFFIC_PER_BATCH = {"pass1_fwd": 25.23e6, "pass2_fwd": 25.49e6, "pass2_bwd": 50.9e6, "pass1_bwd": 50.9e6}
+# q/k/v once). pass_fwd_tc2: read 25.2 MB; pass_bwd_tc: read 51.1-51.3 MB, write 0.4-0.5 MB.
+TRAFFIC_PER_BATCH = {"pass1_fwd": 25.23e6, "pass2_fwd": 25.50e6, "pass2_bwd": 51.88e6, "pass1_bwd": 51.47e6}
 
 
 def peaks():
@@ -545,8 +545,9 @@ def run_module_config(name, args, dev, local_rank):
     else:
         m = P.NPolyAttention(dim=2048, order=3, heads=16, kv_heads=4, dim_head=128, causal=True).to(
             dev, torch.bfloat16)
-        x = torch.randn(32, 2048, 2048, device=dev, dtype=torch.bfloat16)
-        fn, tokens, unit = (lambda: m(x)), 32 * 2048, "tokens/s"
+        pb = args.prefill_batch
+        x = torch.randn(pb, 2048, 2048, device=dev, dtype=torch.bfloat16)
+        fn, tokens, unit = (lambda: m(x)), pb * 2048, "tokens/s"
         flop, fl_note = 8.25e11, "attention core only (order 3, kv-side passes at 4 kv heads); projections excluded"
         out = {"metric": "config 4 NPolyAttention order-3 GQA prefill tokens/s", "dtype": "bf16",
                "config": {"workload": "NPolyAttention(dim=2048 assumed, order 3, h16, g4, d128, causal) fwd, "
@@ -755,6 +756,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-triton", action="store_true", help="skip the reference Triton kernel leg")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1 / 3 / 4-prefill / 5 legs")
+    ap.add_argument("--prefill-batch", type=int, default=32, help="config-4 prefill batch (32; smaller for captures)")
     ap.add_argument("--e2e-chunk", type=int, default=1, help="batch elements per streamed chunk (e2e leg)")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
     ap.add_argument("--decode-batch", type=int, default=32, help="decode leg batch (config 4: 32)")
