@@ -8,8 +8,8 @@ output rows of those chunks.
 
 Forward (causal, reference semantics of poly_attention/poly_attention.py:48-116):
 
-1. start all-gathers of q3, v3 (pass 1's keys / values) and q2 (pass 2's
-   keys); the q2 gather runs while pass 1 computes.
+1. all-gather q3, v3 (pass 1's keys / values) and q2 (pass 2's keys), each
+   into one flat buffer, then reassembled in natural row order.
 2. pass 1 for the own rows of q2 against every key up to the row: one causal
    launch with the key index offset by the chunk start (or, for chunks not a
    multiple of 128 rows, the earlier chunks unmasked plus the diagonal chunk
@@ -59,23 +59,24 @@ def zigzag_unshard(parts, world: int, dim: int = -2) -> torch.Tensor:
 
 
 def _gather_start(x_loc, world, group):
-    """Start an all-gather of this rank's zig-zag shard; returns a handle for
-    _gather_finish (no collective at world size 1)."""
+    """Start an all-gather of this rank's zig-zag shard into one flat
+    [world, ...] buffer; returns a handle for _gather_finish (no collective
+    at world size 1)."""
     x_loc = x_loc.contiguous()
     if world == 1:
-        return [x_loc], None
-    parts = [torch.empty_like(x_loc) for _ in range(world)]
-    work = dist.all_gather(parts, x_loc, group=group, async_op=True)
-    return parts, work
+        return x_loc, None
+    flat = x_loc.new_empty((world * x_loc.shape[0], *x_loc.shape[1:]))   # ranks along dim 0
+    work = dist.all_gather_into_tensor(flat, x_loc, group=group, async_op=True)
+    return flat.view(world, *x_loc.shape), work
 
 
 def _gather_finish(handle, world, dim=-2):
     """Wait for the gather (stream-ordered with NCCL) and reassemble the
     natural row order along `dim`."""
-    parts, work = handle
+    flat, work = handle
     if work is not None:
         work.wait()
-    return parts[0] if world == 1 else zigzag_unshard(parts, world, dim=dim)
+    return flat if world == 1 else zigzag_unshard(list(flat.unbind(0)), world, dim=dim)
 
 
 def _default_ops():
@@ -103,28 +104,45 @@ def context_parallel_order2_fwd(q1_loc, q2_loc, q3_loc, v3_loc, *, group=None, s
     h_q3 = _gather_start(q3_loc, world, group)
     h_v3 = _gather_start(v3_loc, world, group)
     h_q2 = _gather_start(q2_loc, world, group)
+    rows = lambda x, k, dim=-2: x.narrow(dim, k * C, C)   # noqa: E731  (own chunk k of a local shard)
 
+    def diag(q_rows, k, v, bias):
+        """Rows of an own chunk against the same chunk's keys (causal; both
+        index ranges start at the chunk start, so the top-left rule is exact)."""
+        return pass_fn(q_rows, k, v, causal=True, softclamp=sc, bias=bias)
+
+    def prefix(q_rows, c, part, k, v, bias):
+        """Add the keys of the chunks before c (no mask) to a diagonal result."""
+        if c == 0:
+            return part
+        o_p, l_p = pass_fn(q_rows, k[:, :, :c * C], v[:, :, :c * C], causal=False, softclamp=sc,
+                           bias=None if bias is None else bias[:, :, :c * C])
+        return merge_fn(torch.stack([o_p, part[0]]), torch.stack([l_p, part[1]]))
+
+    def whole(q_rows, c, k, v, bias):
+        """Rows of chunk c against keys [0, (c + 1) C) in one causal launch with
+        the key index offset by c * C (C a multiple of the 128-key tile)."""
+        if c == 0:
+            return diag(q_rows, k[:, :, :C], v[:, :, :C], None if bias is None else bias[:, :, :C])
+        return pass_fn(q_rows, k[:, :, :(c + 1) * C], v[:, :, :(c + 1) * C], causal=True, softclamp=sc,
+                       bias=None if bias is None else bias[:, :, :(c + 1) * C], causal_offset=c * C)
+
+    # one offset launch per own chunk (or, for chunks not a multiple of the
+    # 128-key tile, the diagonal block and the earlier chunks merged). Running
+    # the diagonal blocks on local data while the gathers are in flight was
+    # measured slower: the pass kernels hold every SM, so NCCL's gather kernels
+    # wait for them instead of overlapping.
     def attend(q_rows, c, k, v, bias):
-        """Rows of chunk c attend keys [0, (c + 1) C). With C a multiple of the
-        128-key tile this is one causal launch whose key index is offset by
-        c * C; otherwise the diagonal chunk with the causal mask (both index
-        ranges start at c * C, so the top-left rule is exact) and the earlier
-        chunks unmasked, merged."""
-        if c > 0 and C % 128 == 0:
-            return pass_fn(q_rows, k[:, :, :(c + 1) * C], v[:, :, :(c + 1) * C], causal=True, softclamp=sc,
-                           bias=None if bias is None else bias[:, :, :(c + 1) * C], causal_offset=c * C)
-        o, l = pass_fn(q_rows, k[:, :, c * C:(c + 1) * C], v[:, :, c * C:(c + 1) * C], causal=True, softclamp=sc,
-                       bias=None if bias is None else bias[:, :, c * C:(c + 1) * C])
-        if c > 0:
-            o_p, l_p = pass_fn(q_rows, k[:, :, :c * C], v[:, :, :c * C], causal=False, softclamp=sc,
-                               bias=None if bias is None else bias[:, :, :c * C])
-            o, l = merge_fn(torch.stack([o_p, o]), torch.stack([l_p, l]))
-        return o, l
+        if C % 128 == 0:
+            return whole(q_rows, c, k, v, bias)
+        sl = slice(c * C, (c + 1) * C)
+        part = diag(q_rows, k[:, :, sl], v[:, :, sl], None if bias is None else bias[:, :, sl])
+        return prefix(q_rows, c, part, k, v, bias)
 
     # pass 1 for the own rows of q2 (poly_attention/poly_attention.py:63-82)
     q3 = _gather_finish(h_q3, world)
     v3 = _gather_finish(h_v3, world)
-    res = [attend(q2_loc[:, :, k * C:(k + 1) * C], c, q3, v3, None) for k, c in enumerate(own)]
+    res = [attend(rows(q2_loc, k), c, q3, v3, None) for k, c in enumerate(own)]
     del q3, v3
     h_msg = _gather_start(torch.cat([r[0] for r in res], dim=-2), world, group)
     h_lse = _gather_start(torch.cat([r[1] for r in res], dim=-1), world, group)
@@ -134,5 +152,5 @@ def context_parallel_order2_fwd(q1_loc, q2_loc, q3_loc, v3_loc, *, group=None, s
     q2 = _gather_finish(h_q2, world)
     msg = _gather_finish(h_msg, world)
     lse23 = _gather_finish(h_lse, world, dim=-1)
-    outs = [attend(q1_loc[:, :, k * C:(k + 1) * C], c, q2, msg, lse23)[0] for k, c in enumerate(own)]
+    outs = [attend(rows(q1_loc, k), c, q2, msg, lse23)[0] for k, c in enumerate(own)]
     return torch.cat(outs, dim=-2).to(q1_loc.dtype)

@@ -58,7 +58,7 @@ def _worker(rank, world, port, inputs, sc, results):
 @pytest.mark.parametrize("sc", [None, 20.0])
 def test_context_parallel_matches_full_forward(world, sc):
     from poly_attention_b200.distributed import zigzag_unshard
-    b, h, d, C = 1, 2, 16, 6 if world != 2 else 128   # C = 128: the one-launch offset path
+    b, h, d, C = 1, 2, 16, 6 if world != 2 else 128   # C = 128: the one-launch offset path at 2 ranks
     n = 2 * world * C
     g = torch.Generator().manual_seed(world + (sc is not None))
     inputs = [torch.randn(b, h, n, d, generator=g) for _ in range(4)]
