@@ -723,10 +723,11 @@ def run_reference(args, rank):
     def inputs(hs):
         return [torch.randn(1, hs, N, D, generator=g) for _ in range(5)]
 
+    reference_cpu_step(refmod, inputs(1))          # first call: allocator and thread-pool start-up
     t0 = time.perf_counter()
-    reference_cpu_step(refmod, inputs(1))
-    one = time.perf_counter() - t0
-    hs = int(max(1, min(H, 200.0 / (max(one, 1e-3) * (args.steps + args.warmup)))))
+    reference_cpu_step(refmod, inputs(2))
+    per_head = (time.perf_counter() - t0) / 2
+    hs = int(max(1, min(H, 200.0 / (max(per_head, 1e-3) * (args.steps + args.warmup)))))
     ins = inputs(hs)
     for _ in range(args.warmup):
         reference_cpu_step(refmod, ins)
