@@ -35,6 +35,7 @@ class ModuleKVCache:
         self.api_lses = [torch.empty(batch, heads, capacity, device=device, dtype=dtype) for _ in range(order - 1)]
         self.api_msgs = [torch.empty(batch, heads, capacity, dim_head, device=device, dtype=dtype)
                          for _ in range(order - 1)]
+        self.last = None   # the tuple object last returned for the current views
 
     @property
     def length(self):
@@ -77,12 +78,17 @@ class ModuleKVCache:
                 self._mirror(i, slice(0, n))
         self.dec.length = n
 
-    def _mirror(self, i, rows):
+    def _mirror_pairs(self, i, rows):
+        """(destination, source) of the h-head mirrors of level i's rows."""
         b, g, r = self.b, self.g, self.r
         lg, mg = self.dec.lses[i][:, :, rows], self.dec.msgs[i][:, :, rows]
         n = lg.shape[-1]
-        self.api_lses[i][:, :, rows].view(b, g, r, n).copy_(lg[:, :, None].expand(b, g, r, n))
-        self.api_msgs[i][:, :, rows].view(b, g, r, n, self.d).copy_(mg[:, :, None].expand(b, g, r, n, self.d))
+        return ((self.api_lses[i][:, :, rows].view(b, g, r, n), lg[:, :, None].expand(b, g, r, n)),
+                (self.api_msgs[i][:, :, rows].view(b, g, r, n, self.d), mg[:, :, None].expand(b, g, r, n, self.d)))
+
+    def _mirror(self, i, rows):
+        for dst, src in self._mirror_pairs(i, rows):
+            dst.copy_(src)
 
     @classmethod
     def from_core(cls, keys, vals, lses_g, msgs_g, *, heads, capacity=None, softclamp_value=None):
@@ -125,9 +131,16 @@ class ModuleKVCache:
         L = self.length
         self.dec.append_kv(keys_new, vals_new)
         out = self.dec.step(q1)
-        for i in range(self.order - 1):
-            self._mirror(i, slice(L, L + 1))
+        pairs = [pr for i in range(self.order - 1) for pr in self._mirror_pairs(i, slice(L, L + 1))]
+        torch._foreach_copy_([d for d, _ in pairs], [s_ for _, s_ in pairs])   # all mirror rows, few launches
+        self.last = None
         return out
+
+    def remember(self, cache):
+        """Note the tuple object handed out for the current views (a cheap
+        identity check for the next step; `owns` is the full check)."""
+        self.last = cache
+        return cache
 
 
 def usable(dtype, device, dim_head, has_masks, has_rotary):

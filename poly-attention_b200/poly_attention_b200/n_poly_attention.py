@@ -131,7 +131,7 @@ class NPolyAttention(Module):
             # the tuple is not the one this module returned last)
             c_qs, c_vs, c_lses, c_msgs = cache
             kv = self._kv_cache
-            if kv is None or not kv.owns(list(c_qs), list(c_vs), list(c_lses), list(c_msgs)):
+            if kv is None or (cache is not kv.last and not kv.owns(list(c_qs), list(c_vs), list(c_lses), list(c_msgs))):
                 kv = ModuleKVCache.from_tuple(list(c_qs), list(c_vs), list(c_lses), list(c_msgs), heads=self.heads,
                                               softclamp_value=self.softclamp_value)
             if kv.length >= kv.cap:
@@ -141,7 +141,7 @@ class NPolyAttention(Module):
             if not return_cache:
                 return out
             k, v, l, m = kv.views()
-            return out, (tuple(k), tuple(v), tuple(l), tuple(m))
+            return out, kv.remember((tuple(k), tuple(v), tuple(l), tuple(m)))
         if has_cache:
             c_qs, c_vs, c_lses, c_msgs = cache
         else:
@@ -175,7 +175,7 @@ class NPolyAttention(Module):
                                          heads=self.heads, softclamp_value=self.softclamp_value)
             self._kv_cache = kv
             k, v, l, m = kv.views()
-            return out, (tuple(k), tuple(v), tuple(l), tuple(m))
+            return out, kv.remember((tuple(k), tuple(v), tuple(l), tuple(m)))
         new_lses, new_msgs = [], []
         for i, (l, m) in enumerate(zip(lse_steps, msg_steps)):
             l = self._expand(l).to(out.dtype)

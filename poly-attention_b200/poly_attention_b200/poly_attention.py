@@ -164,7 +164,7 @@ class Order2PolyAttention(Module):
             # append in place to the module's cache buffers (a copy first if
             # the tuple is not the one this module returned last)
             kv = self._kv_cache
-            if kv is None or not kv.owns([cq2, cq3], [cv3], [clse23], [cmsg]):
+            if kv is None or (cache is not kv.last and not kv.owns([cq2, cq3], [cv3], [clse23], [cmsg])):
                 kv = ModuleKVCache.from_tuple([cq2, cq3], [cv3], [clse23], [cmsg], heads=self.heads,
                                               softclamp_value=self.softclamp_value)
             if kv.length >= kv.cap:
@@ -175,7 +175,7 @@ class Order2PolyAttention(Module):
             if not return_cache:
                 return out
             k, v, l, m = kv.views()
-            return out, (k[0], k[1], v[0], l[0], m[0])
+            return out, kv.remember((k[0], k[1], v[0], l[0], m[0]))
         cat = lambda c, t: t if c is None else torch.cat((c, t), dim=-2)  # noqa: E731
         q2_cache, q3_cache, v3_cache = cat(cq2, q2), cat(cq3, q3), cat(cv3, v3)
 
@@ -204,7 +204,7 @@ class Order2PolyAttention(Module):
                                          softclamp_value=self.softclamp_value)
             self._kv_cache = kv
             k, v, l, m = kv.views()
-            return out, (k[0], k[1], v[0], l[0], m[0])
+            return out, kv.remember((k[0], k[1], v[0], l[0], m[0]))
         lse_step = self._expand(lse_step).to(out.dtype)
         msg_step = self._expand(msg_step)
         lse23_full = lse_step if clse23 is None else torch.cat((clse23, lse_step), dim=-1)
