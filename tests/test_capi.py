@@ -50,6 +50,16 @@ def test_invalid_args_report_errors_without_gpu():
     assert "divisible" in _lib.lib.poly_last_error().decode()
     a.heads, a.head_dim = 2, 512
     assert _lib.lib.poly_pass_fwd(ctypes.byref(a), None) == _lib.POLY_EUNSUPPORTED
+    # causal_offset: negative is invalid; non-zero is refused (before any launch)
+    # outside the tcgen05 forward, here an fp32 pass
+    a.head_dim, a.q, a.k, a.v, a.out = 64, 256, 256, 256, 256
+    a.causal, a.causal_offset = 1, -128
+    assert _lib.lib.poly_pass_fwd(ctypes.byref(a), None) == _lib.POLY_EINVAL
+    assert "causal_offset" in _lib.lib.poly_last_error().decode()
+    a.dtype, a.causal_offset = _lib.POLY_F32, 128
+    assert _lib.lib.poly_pass_fwd(ctypes.byref(a), None) == _lib.POLY_EUNSUPPORTED
+    assert "causal_offset" in _lib.lib.poly_last_error().decode()
+    a.causal_offset, a.q, a.k, a.v, a.out, a.head_dim = 0, None, None, None, None, 512
     # poly_copy_rows validates every copy before launching
     rc = _lib.PolyRowCopy()
     assert _lib.lib.poly_copy_rows(None, 1, None) == _lib.POLY_EINVAL
