@@ -64,12 +64,13 @@ unsigned long long poly_launch_count(void) { return g_launches.load(std::memory_
 
 int poly_device_error(int* out, int reset) {
   if (!out) return fail(POLY_EINVAL, "null out");
-  int a = 0, b = 0, c = 0, d = 0;
+  int a = 0, b = 0, c = 0, d = 0, e = 0;
   int rc = read_device_error_fwd(&a, reset != 0);
   if (!rc) rc = read_device_error_fwd2(&c, reset != 0);
   if (!rc) rc = read_device_error_bwd(&b, reset != 0);
   if (!rc) rc = read_device_error_dec(&d, reset != 0);
-  *out = a ? a : (c ? c : (b ? b : d));
+  if (!rc) rc = read_device_error_bwd128(&e, reset != 0);
+  *out = a ? a : (c ? c : (b ? b : (d ? d : e)));
   return rc;
 }
 int poly_selftest_wait_timeout(unsigned long long limit_ns, int* result, void* stream) {

@@ -70,6 +70,9 @@ int read_device_error_fwd(int* out, bool reset);
 int read_device_error_bwd(int* out, bool reset);
 int read_device_error_fwd2(int* out, bool reset);
 int read_device_error_dec(int* out, bool reset);
+int read_device_error_bwd128(int* out, bool reset);
+size_t pass_bwd_tc128_workspace(const PolyPassBwdArgs& a);
+int launch_pass_bwd_tc128(const PolyPassBwdArgs& a, cudaStream_t s);
 int selftest_wait_timeout(uint64_t limit_ns, int* result, cudaStream_t s);
 bool pass_fwd_tc2_eligible(const PolyPassArgs& a);
 int launch_pass_fwd_tc2(const PolyPassArgs& a, cudaStream_t s);

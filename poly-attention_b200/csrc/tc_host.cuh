@@ -52,17 +52,17 @@ inline int make_map(CUtensorMap* m, const void* base, int dtype, int d, int rows
   return POLY_OK;
 }
 
-// 3-D fp32 map over a contiguous [planes][rows][64] accumulator, box 32 x 128,
-// 128-byte swizzle (used for TMA reduce-add of dQ tiles).
-inline int make_map_f32_acc(CUtensorMap* m, float* base, int rows, int planes) {
+// 3-D fp32 map over a contiguous [planes][rows][cols] accumulator, box 32 x
+// box_rows, 128-byte swizzle (used for TMA reduce-add of dQ tiles).
+inline int make_map_f32_acc(CUtensorMap* m, float* base, int rows, int planes, int cols = 64, int box_rows = 128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is unavailable");
     return POLY_ECUDA;
   }
-  const cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)planes};
-  const cuuint64_t strides[2] = {64 * 4, (cuuint64_t)rows * 64 * 4};
-  const cuuint32_t box[3] = {32, 128, 1};
+  const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)planes};
+  const cuuint64_t strides[2] = {(cuuint64_t)cols * 4, (cuuint64_t)rows * cols * 4};
+  const cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
   const cuuint32_t es[3] = {1, 1, 1};
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

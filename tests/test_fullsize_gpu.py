@@ -132,3 +132,45 @@ def test_config3_polyvit_full(golden, dtype):
         np.testing.assert_allclose(host(y), gd["y"], atol=1e-4, rtol=0)
     else:
         np.testing.assert_allclose(host(y), gd["y"], atol=BF16_ATOL, rtol=BF16_RTOL)
+
+
+def test_chain_order3_d128_backward_sampled():
+    """Order-3 chain gradients at config 4's head size (d = 128, 16 query / 4
+    kv heads, causal, bf16), the training path of NPolyAttention at that size:
+    the tcgen05 head_dim-128 backward, checked on 2 sequences against the
+    oracle's chain backward (n_poly_attention.py:233-313, reversed)."""
+    import poly_attention_b200 as P
+    b, h, g, n, d = 4, 16, 4, 1024, 128
+    gen = torch.Generator(device="cuda").manual_seed(128)
+    mk = lambda heads: torch.randn(b, heads, n, d, device="cuda", dtype=torch.bfloat16,  # noqa: E731
+                                   generator=gen).requires_grad_(True)
+    q1 = mk(h)
+    ql_rest = [mk(g), mk(g)]           # q2, q3 (left queries of levels 1, 2)
+    qr = [mk(g), mk(g), mk(g)]         # keys of levels 0..2
+    vs = [mk(g), mk(g)]
+    out, _, _ = P.poly_attention_chain([q1, *ql_rest], qr, vs, causal=True)
+    do = torch.randn(out.shape, device="cuda", dtype=torch.bfloat16, generator=gen)
+    out.backward(do)
+    torch.cuda.synchronize()
+    ts = [q1, *ql_rest, *qr, *vs]
+    for bi in (0, 3):
+        sl = lambda t: host(t[bi:bi + 1])  # noqa: E731
+        r = h // g
+        rep_ = lambda a: np.repeat(a, r, 1)  # noqa: E731
+        ql_np = [sl(q1), rep_(sl(ql_rest[0])), rep_(sl(ql_rest[1]))]
+        qr_np = [rep_(sl(t)) for t in qr]
+        vs_np = [rep_(sl(t)) for t in vs]
+        grads = O.npoly_chain_bwd(ql_np, qr_np, vs_np, host(do[bi:bi + 1]), causal=True)
+        dql, dqr, dvs = grads[0], grads[1], grads[2]
+        group = lambda a: a.reshape(1, g, r, n, d).sum(2)  # noqa: E731
+        want = [dql[0], group(dql[1]), group(dql[2]), *[group(x) for x in dqr], *[group(x) for x in dvs]]
+        for i, (t, w) in enumerate(zip(ts, want)):
+            got = sl(t.grad)
+            err = np.abs(got - w)
+            # the stated bf16 bound on all but 1e-4 of the elements; every element
+            # within 2x it: the value gradients of the deeper levels are bf16
+            # products dv * msg of tensors up to ~10 in magnitude (as in the
+            # reference's bf16 module), whose rounding alone reaches ~0.04
+            over = err > BF16_ATOL + BF16_RTOL * np.abs(w)
+            assert over.mean() <= 1e-4, f"grad {i} seq {bi}: {over.sum()} elements over the bf16 bound"
+            np.testing.assert_allclose(got, w, atol=2 * BF16_ATOL, rtol=2 * BF16_RTOL, err_msg=f"grad {i} seq {bi}")

@@ -292,10 +292,11 @@ def test_tc_forward_selected_and_matches(d, causal, n):
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("n,g", [(300, 2), (1024, 4)])
 @pytest.mark.parametrize("softclamp", [None, 20.0])
-def test_tc_backward_selected_and_matches(causal, n, g, softclamp):
-    """bf16 / fp16 with d = 64 must run the tcgen05 backward; grads vs oracle."""
+@pytest.mark.parametrize("d", [64, 128])
+def test_tc_backward_selected_and_matches(causal, n, g, softclamp, d):
+    """bf16 / fp16 with d = 64 or 128 must run a tcgen05 backward; grads vs oracle."""
     import poly_attention_b200 as P
-    b, h, d = 1, 4, 64
+    b, h = 1, 4
     r = h // g
     for dtype in (torch.bfloat16, torch.float16):
         q = quant(rnd((b, h, n, d), 1), dtype)
@@ -334,13 +335,14 @@ def test_tc_backward_selected_and_matches(causal, n, g, softclamp):
 
 @pytest.mark.parametrize("nq,nk", [(384, 300), (128, 200), (300, 384), (257, 129)])
 @pytest.mark.parametrize("causal", [False, True])
-def test_tc_ragged_without_bias(nq, nk, causal):
+@pytest.mark.parametrize("d", [64, 128])
+def test_tc_ragged_without_bias(nq, nk, causal, d):
     """Ragged key tails without a bias take the kernels' tail-masking path."""
     import poly_attention_b200 as P
     dtype = torch.bfloat16
-    q = quant(rnd((1, 2, nq, 64), 1), dtype)
-    k, v = (quant(rnd((1, 2, nk, 64), s), dtype) for s in (2, 3))
-    do = quant(rnd((1, 2, nq, 64), 4), dtype)
+    q = quant(rnd((1, 2, nq, d), 1), dtype)
+    k, v = (quant(rnd((1, 2, nk, d), s), dtype) for s in (2, 3))
+    do = quant(rnd((1, 2, nq, d), 4), dtype)
     qt, kt, vt = dev(q, dtype), dev(k, dtype), dev(v, dtype)
     assert P.kernel_names(qt, kt, vt, causal=causal) == ("tc100", "tc100")
     out, lse = P.pass_fwd(qt, kt, vt, causal=causal)
@@ -348,8 +350,8 @@ def test_tc_ragged_without_bias(nq, nk, causal):
     assert_close(out, eo, dtype, "out")
     assert_close(lse, el, dtype, "lse")
     dq, dk, dv, _ = P.pass_bwd(qt, kt, vt, out, lse, dev(do, dtype), causal=causal)
-    e = O._pass_bwd(q, k, v, do, scale=0.125, causal=causal, softclamp_value=None, key_mask=None, query_mask=None,
-                    bias=None)
+    e = O._pass_bwd(q, k, v, do, scale=d ** -0.5, causal=causal, softclamp_value=None, key_mask=None,
+                    query_mask=None, bias=None)
     assert_close(dq, e[0], dtype, "dq")
     assert_close(dk, e[1], dtype, "dk")
     assert_close(dv, e[2], dtype, "dv")
@@ -371,14 +373,15 @@ def test_polyvit_golden(golden, order):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("d", [32, 128])
 def test_pass_bwd_other_head_dims(dtype, d):
-    """Backward at head sizes the tensor-core backward does not take (CUDA-core path)."""
+    """Backward at other head sizes: d = 32 (and fp32) on the CUDA cores, d = 128
+    bf16 on the head_dim-128 tcgen05 kernel (70 rows: one partial tile)."""
     import poly_attention_b200 as P
     b, h, g, n = 1, 4, 2, 70
     q = quant(rnd((b, h, n, d), 1), dtype)
     k, v = (quant(rnd((b, g, n, d), s), dtype) for s in (2, 3))
     do = quant(rnd((b, h, n, d), 4), dtype)
     qt, kt, vt = dev(q, dtype), dev(k, dtype), dev(v, dtype)
-    assert P.kernel_names(qt, kt, vt, causal=True)[1] == "simt"
+    assert P.kernel_names(qt, kt, vt, causal=True)[1] == ("tc100" if d == 128 and dtype != torch.float32 else "simt")
     out, lse = P.pass_fwd(qt, kt, vt, causal=True)
     dq, dk, dv, _ = P.pass_bwd(qt, kt, vt, out, lse, dev(do, dtype), causal=True)
     r = h // g
