@@ -329,7 +329,7 @@ def run_ours(args, rank, world, local_rank):
     configs = {}
     if not args.no_configs:
         if world == 1:
-            for name in ("config1", "vit", "prefill4"):
+            for name in ("config1", "vit", "prefill4", "chain_train_d128"):
                 configs[name] = run_module_config(name, args, dev, local_rank)
                 torch.cuda.empty_cache()
         # config 5: one GPU alone, or keys split across all ranks (one NCCL exchange)
@@ -515,6 +515,51 @@ def run_longctx(args, rank, world, local_rank):
             "clocks": clk, "gpu_launches_per_rank": int(launches / max(args.steps, 1))}
 
 
+def run_chain_train(args, dev, local_rank):
+    """Order-3 chain forward + backward at config 4's head shape (16 query /
+    4 kv heads, d 128, causal, bf16), batch 8 x 2048 tokens: the training
+    path of NPolyAttention at that size (not a BASELINE metric; config 4 is
+    inference). Runs on the tcgen05 forward and the head_dim-128 backward."""
+    import torch
+
+    import poly_attention_b200 as P
+    from poly_attention_b200 import _lib
+    b, h, g, n, d = args.chain_batch, 16, 4, 2048, 128
+    gen = torch.Generator(device=dev).manual_seed(9)
+    mk = lambda heads: torch.randn(b, heads, n, d, device=dev, dtype=torch.bfloat16,  # noqa: E731
+                                   generator=gen).requires_grad_(True)
+    q1, q2, q3, k1, k2, k3, v1, v2 = mk(h), mk(g), mk(g), mk(g), mk(g), mk(g), mk(g), mk(g)
+    do = torch.randn(b, h, n, d, device=dev, dtype=torch.bfloat16, generator=gen)
+    leaves = (q1, q2, q3, k1, k2, k3, v1, v2)
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        out, _, _ = P.poly_attention_chain([q1, q2, q3], [k1, k2, k3], [v1, v2], causal=True)
+        out.backward(do)
+
+    for _ in range(args.warmup):
+        step()
+    n0 = _lib.launch_count()
+    ms, clk = timed_region(step, args.steps, dev, 1, local_rank)
+    launches = _lib.launch_count() - n0
+    # causal pass: 2 GEMMs x 2 n^2 d / 2; two levels at kv-head width, the last at h
+    # heads; backward counts 2x the forward
+    fwd = 2 * 2 * (n * n / 2) * d * b * (g + g + h)
+    flop = 3 * fwd
+    _, burst, _, kind = peaks()
+    tf = flop / (ms * 1e-3) / 1e12
+    return {"metric": "order-3 chain fwd+bwd tokens/s at config 4's head shape", "value": b * n / (ms * 1e-3),
+            "unit": "tokens/s", "ms_per_step": ms, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "dtype": "bf16", "data": "synthetic N(0,1), seeded", "higher_is_better": True, "vs_baseline": None,
+            "config": {"workload": "poly_attention_chain order 3, causal, fwd + bwd (training path, not a BASELINE "
+                                   "config)", "batch": b, "heads": h, "kv_heads": g, "seq_len": n, "dim_head": d},
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": burst, "unit": "TFLOP/s", "frac": tf / burst,
+                         "peak_kind": f"{kind} bf16 burst",
+                         "flop_note": "3 causal passes (2 at 4 kv heads, 1 at 16) fwd, bwd counted 2x"},
+            "clocks": clk, "gpu_launches_per_step": int(launches / max(args.steps, 1))}
+
+
 def run_module_config(name, args, dev, local_rank):
     """Configs 1, 3 and the config-4 prefill through the drop-in modules
     (projections / norms / MLPs in PyTorch, attention cores in libpolyattn)."""
@@ -522,6 +567,8 @@ def run_module_config(name, args, dev, local_rank):
 
     import poly_attention_b200 as P
     from poly_attention_b200 import _lib
+    if name == "chain_train_d128":
+        return run_chain_train(args, dev, local_rank)
     torch.manual_seed(0)
     sustained, burst, _, kind = peaks()
     if name == "config1":
@@ -757,12 +804,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-triton", action="store_true", help="skip the reference Triton kernel leg")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1 / 3 / 4-prefill / 5 legs")
+    ap.add_argument("--chain-batch", type=int, default=8, help="batch of the chain_train_d128 leg")
     ap.add_argument("--prefill-batch", type=int, default=32, help="config-4 prefill batch (32; smaller for captures)")
     ap.add_argument("--e2e-chunk", type=int, default=1, help="batch elements per streamed chunk (e2e leg)")
     ap.add_argument("--no-decode", action="store_true", help="skip the KV-cache decode leg")
     ap.add_argument("--decode-batch", type=int, default=32, help="decode leg batch (config 4: 32)")
     ap.add_argument("--decode-cache", type=int, default=2048, help="decode leg prefilled cache length (config 4: 2048)")
-    ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4", "decode", "triton_ref"],
+    ap.add_argument("--workload", choices=["train", "longctx", "config1", "vit", "prefill4", "chain_train_d128", "decode",
+                                           "triton_ref"],
                     default="train", help="train: everything (the default line); the others run one leg alone")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -786,7 +835,7 @@ def main():
             res = res if rank == 0 else None
         elif args.workload == "decode":
             res = run_decode(args, dev) if rank == 0 else None
-        elif args.workload in ("config1", "vit", "prefill4"):
+        elif args.workload in ("config1", "vit", "prefill4", "chain_train_d128"):
             res = run_module_config(args.workload, args, dev, local_rank) if rank == 0 else None
         else:
             res = run_ours(args, rank, world, local_rank)
